@@ -1,0 +1,376 @@
+"""Benchmark of the Q6W hot path: batched greedy decode of the tiny model.
+
+Workload (one "step" = one full pass of the path over one batch): every
+rank serves its own 8192 independent requests of the tiny synthetic model
+(dim 128, 5 layers, 8 q heads, 4 kv heads, head_dim 16, SwiGLU hidden 384,
+vocab 4096, FP32 KV cache of 256 positions; weights N(0, 0.02) from seed
+1234, Q6W-quantized), each a 20-token prompt drawn U[3, 4095] (seeded by
+rank) prefilled token by token and followed by 128 greedy tokens.  Ranks
+share nothing (pure data parallelism, weak scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W]
+  python bench.py --impl reference ...   # the reference's CPU path (oracle port), rank 0 only
+
+Prints one JSON line on rank 0.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "tinyllm-pynq-z2_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "generated tok/s (batched greedy decode, tiny Q6W model)"
+SEED = 1234
+VOCAB_LO = 3
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--n-seqs", type=int, default=8192, help="sequences per GPU")
+    ap.add_argument("--prompt-len", type=int, default=20)
+    ap.add_argument("--new-tokens", type=int, default=128)
+    ap.add_argument("--cpu-sample-requests", type=int, default=2, help="requests per CPU worker per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def make_model_files(d):
+    from q6w_b200 import format as fmt
+
+    b, m = Path(d) / "tiny.bin", Path(d) / "tiny.json"
+    fmt.write_synthetic(fmt.TINY_ARGS, SEED, b, m)
+    return b, m
+
+
+def prompts_for(rank, n, length):
+    import torch
+
+    g = torch.Generator().manual_seed(10_000 + rank)
+    return torch.randint(VOCAB_LO, 4096, (n, length), generator=g, dtype=torch.int64).to(torch.int32)
+
+
+# ---------------------------------------------------------------- CPU side --
+
+def _cpu_worker(args):
+    """One process: B=1 greedy requests through the oracle port of the
+    reference's CachedTransformer.step loop, single-threaded."""
+    bin_path, man_path, prompts, new_tokens = args
+    import torch
+
+    torch.set_num_threads(1)
+    from oracle.model import OracleModel, greedy_request
+
+    m = OracleModel.from_q6w(bin_path, man_path)
+    greedy_request(m, prompts[0], 4)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    for p in prompts:
+        n += len(greedy_request(m, p, new_tokens)["generated"])
+    return n, time.perf_counter() - t0
+
+
+def cpu_throughput(bin_path, man_path, prompt_rows, new_tokens, workers, per_worker, pool=None):
+    """Aggregate tok/s of `workers` single-threaded processes (one request stream each)."""
+    import multiprocessing as mp
+
+    jobs = []
+    for w in range(workers):
+        rows = [prompt_rows[(w * per_worker + i) % len(prompt_rows)] for i in range(per_worker)]
+        jobs.append((str(bin_path), str(man_path), rows, new_tokens))
+    own = pool is None
+    if own:
+        pool = mp.get_context("spawn").Pool(workers)
+    try:
+        t0 = time.perf_counter()
+        res = pool.map(_cpu_worker, jobs)
+        wall = time.perf_counter() - t0
+    finally:
+        if own:
+            pool.close()
+            pool.join()
+    toks = sum(r[0] for r in res)
+    busy = max(r[1] for r in res)
+    return toks / busy, toks, busy, wall
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(a):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    with tempfile.TemporaryDirectory() as d:
+        b, m = make_model_files(d)
+        prompts = prompts_for(0, 4096, a.prompt_len).tolist()
+        cores = cpu_cores()
+        import multiprocessing as mp
+
+        pool = mp.get_context("spawn").Pool(cores)
+        try:
+            for _ in range(max(0, a.warmup)):
+                cpu_throughput(b, m, prompts, a.new_tokens, cores, 1, pool)
+            samples = [cpu_throughput(b, m, prompts, a.new_tokens, cores, 1, pool) for _ in range(a.steps)]
+        finally:
+            pool.close()
+            pool.join()
+    value = statistics.median(s[0] for s in samples)
+    per_step_ms = statistics.median(s[2] for s in samples) * 1e3
+    sample = (f"{cores} single-thread processes x 1 request (prompt {a.prompt_len} + {a.new_tokens} greedy "
+              f"tokens, B=1 cached-step loop) per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(per_step_ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(a, world),
+        "cpu_baseline": {"value": round(value, 2), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(a, world):
+    return {"workload": (f"batched greedy decode, tiny Q6W model (dim 128, 5 layers, 8 q / 4 kv heads, hd 16, "
+                         f"hidden 384, vocab 4096, ctx 256): {a.n_seqs} sequences per GPU x ({a.prompt_len}-token "
+                         f"prompt + {a.new_tokens} generated), FP32 KV cache"),
+            "sequences_per_gpu": a.n_seqs, "prompt_len": a.prompt_len, "new_tokens": a.new_tokens,
+            "global_sequences": a.n_seqs * world, "parallelism": f"dp{world} (independent replicas, no collectives)",
+            "l2": "inputs larger than L2: per-GPU KV cache 5.4 GB rewritten every step"}
+
+
+# ---------------------------------------------------------------- GPU side --
+
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def run_b200(a):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    from q6w_b200.model import Q6WCudaTransformer
+
+    tmp = tempfile.TemporaryDirectory()
+    b, m = make_model_files(tmp.name)
+    model = Q6WCudaTransformer.from_q6w(b, m, device=dev)
+    n, P, T = a.n_seqs, a.prompt_len, a.new_tokens
+    host_prompts = prompts_for(rank, n, P).pin_memory()
+    prompts = host_prompts.to(dev)
+    lens = torch.full((n,), P, dtype=torch.int32, device=dev)
+    caches = model.new_batch_cache(n)
+    out_host = torch.empty((n, T), dtype=torch.int32).pin_memory()
+
+    def one(prompts_dev):
+        return model.generate_greedy_device(prompts_dev, lens, P, T, caches=caches)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up (also captures the step graph)
+    for _ in range(max(a.warmup, 1)):
+        sampled, n_sampled, stop_reason, _, _, ws = one(prompts)
+    model.check_device_status(ws)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    # ---- device-resident timed region
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(dev.index)
+    barrier()
+    torch.cuda.synchronize()
+    with clk:
+        start.record(stream)
+        for _ in range(a.steps):
+            one(prompts)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(stop)
+    clocks = clk.summary()
+
+    # ---- end-to-end: pinned host prompts in, generated ids out, every step
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(a.steps):
+        pd = host_prompts.to(dev, non_blocking=True)
+        sampled, *_ = one(pd)
+        out_host.copy_(sampled, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # ---- correctness of the timed output: full length and a teacher-forced oracle check on a sample
+    ok_len = bool((n_sampled == T).all().item())
+
+    # ---- dominant kernel alone: decode attention over this run's caches
+    roof = attention_roofline(model, caches, n, P + T - 1, stream)
+
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    total_tokens = n * T * a.steps * world
+    value = total_tokens / (ms / 1e3)
+    e2e_value = total_tokens / (e2e_ms / 1e3)
+    launches_per_gen = 1 + (P + T - 1) * (1 + 5 * model.args.n_layers + 2)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(a, world),
+            "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(n * P * 4),
+                    "d2h_bytes_per_step": int(n * T * 4)},
+            "gpu_launches": launches_per_gen * a.steps,
+            "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len,
+        }
+        if not a.no_cpu_baseline and world == 1:
+            cores = cpu_cores()
+            rows = host_prompts[: 4 * cores].tolist()
+            v, toks, busy, wall = cpu_throughput(b, m, rows, T, cores, a.cpu_sample_requests)
+            line["cpu_baseline"] = {"value": round(v, 2), "unit": "tok/s", "cores": cores, "kind": "port",
+                                    "sample": f"{cores} single-thread processes x {a.cpu_sample_requests} requests "
+                                              f"({P}+{T} tokens, B=1 cached-step loop of the oracle port); "
+                                              f"{toks} tokens in {busy:.1f} s"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    tmp.cleanup()
+
+
+def attention_roofline(model, caches, n, length, stream):
+    """Time the decode-attention kernel alone (public op, one layer of this
+    run's caches at the final length) and report its HBM roofline.
+
+    Algorithmic bytes per launch = K and V rows read (n * length * kv_heads *
+    head_dim * 4 bytes each) + queries in + outputs out.
+    """
+    import torch
+
+    from q6w_b200 import ops
+
+    k, v = caches
+    a = model.args
+    H, KV, hd = a.n_heads, model.n_kv_heads, model.head_dim
+    kl = k[:, 0]  # layer 0 view: [n, max_seq, KV, hd], sequence stride = whole cache
+    vl = v[:, 0]
+    q = torch.randn(n, H, hd, device=k.device)
+    lens = torch.full((n,), length, dtype=torch.int32, device=k.device)
+    for _ in range(3):
+        ops.gqa_attention(q, kl, vl, lens, H // KV)
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        ops.gqa_attention(q, kl, vl, lens, H // KV)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    nbytes = 2 * n * length * KV * hd * 4 + 2 * n * H * hd * 4
+    peak, kind = measured_peaks()
+    ach = nbytes / sec / 1e9
+    return {"kernel": "attn_kernel (decode GQA attention, timed alone)", "bound": "hbm", "achieved": round(ach, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": f"{kind} hbm_gbs",
+            "traffic": None, "bytes_per_launch": nbytes, "us_per_launch": round(sec * 1e6, 2)}
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_b200(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/*
+ * q6w_b200.h -- C ABI of the B200 (sm_100a) Q6W inference hot path.
+ *
+ * Q6W: signed int6 weights, one FP32 scale per output row, four values
+ * packed low-bit-first into three bytes, rows stored row-major exactly as in
+ * the reference file format (quantization/q6w_format.py:52-64, 101-227).
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer owned by the caller, unless
+ *     the comment says "host".  Nothing here allocates device memory except
+ *     the decode-graph cache kept inside a q6w_model (see q6w_generate_greedy).
+ *   - Matrices are row-major; a Q6W matrix of [rows, cols] occupies
+ *     rows*cols*3/4 bytes, cols % 4 == 0.
+ *   - The last argument is the CUDA stream the work is enqueued on (pass
+ *     0 for the legacy default stream).  Calls are asynchronous.
+ *   - Every entry point returns Q6W_OK (0) or a negative status and never
+ *     traps; q6w_last_error() gives a message for the calling host thread.
+ *     This replaces the reference's silent early returns on bad arguments
+ *     (scripts/neon_gqa_attention.c:15-19) and mirrors the status -1 of the
+ *     HLS top (rtl/autonomous/tinyllm_autonomous.cpp:1093-1099).
+ */
+#ifndef Q6W_B200_H
+#define Q6W_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define Q6W_API __attribute__((visibility("default")))
+#else
+#define Q6W_API
+#endif
+
+typedef struct CUstream_st* q6w_stream_t; /* == cudaStream_t */
+
+enum {
+  Q6W_OK = 0,
+  Q6W_ERR_ARG = -1,      /* bad shape / null pointer / unsupported size   */
+  Q6W_ERR_ALIGN = -2,    /* pointer not aligned as required               */
+  Q6W_ERR_RANGE = -3,    /* token or position outside the model's range   */
+  Q6W_ERR_CUDA = -4,     /* a CUDA runtime call failed                    */
+  Q6W_ERR_DEVICE = -5    /* a kernel flagged bad device-side input        */
+};
+
+/* Message for the last failing call on this host thread ("" if none). */
+Q6W_API const char* q6w_last_error(void);
+/* ABI version, bumped on any incompatible change. */
+Q6W_API int32_t q6w_abi_version(void);
+
+/* ---- codec ------------------------------------------------------------- */
+
+/* Decode packed Q6W rows to int8 codes in [-32, 31].
+ * Replaces unpack_signed_int6 (quantization/q6w_format.py:67-81). */
+Q6W_API int32_t q6w_unpack(const uint8_t* packed, int8_t* out, int64_t rows, int64_t cols,
+                   q6w_stream_t stream);
+
+/* out[r, c] = float(q[r, c]) * scales[r], one rounded FP32 product per
+ * element -- bit-identical to the reference dequantization
+ * (quantization/q6w_format.py:257-259). */
+Q6W_API int32_t q6w_dequant(const uint8_t* packed, const float* scales, float* out, int64_t rows,
+                    int64_t cols, q6w_stream_t stream);
+
+/* ---- linear ------------------------------------------------------------ */
+
+/* y[n, rows] = x[n, cols] @ W^T with W = dequant(packed, scales): the
+ * nn.Linear calls of the cached step (benchmarks/torch_benchmark.py:105-107,
+ * 121, 123, 125) on Q6W weights, FP32 accumulation.  x and y are row-major
+ * FP32, 4-byte aligned; n >= 0 (n == 0 is a no-op). */
+Q6W_API int32_t q6w_linear(const uint8_t* packed, const float* scales, const float* x, float* y,
+                   int64_t rows, int64_t cols, int64_t n, q6w_stream_t stream);
+
+/* Vocab projection + greedy pick: logits = x @ W^T (optional, may be NULL)
+ * and argmax[n] = first index of each row's maximum (torch.argmax), fused --
+ * the tied-embedding classifier of torch_benchmark.py:125 with the greedy
+ * sample_token of :148-150.  Replaces arm_neon_q6_vocab_sgemv_f32
+ * (scripts/neon_q6_vocab.c:12-88) plus the host argmax.  `scratch` is
+ * caller-owned device memory of >= 8*n bytes (8-byte aligned), overwritten.
+ * Needs cols % 16 == 0, even rows, 16-byte aligned x. */
+Q6W_API int32_t q6w_linear_argmax(const uint8_t* packed, const float* scales, const float* x,
+                                  float* logits, int32_t* argmax, void* scratch,
+                                  size_t scratch_bytes, int64_t rows, int64_t cols, int64_t n,
+                                  q6w_stream_t stream);
+
+/* out[s, :] = x[s, :] * (1 / sqrt(mean(x[s, :]^2) + eps)) * weight, for n
+ * rows of `length` (torch_benchmark.py:22-24).  Replaces
+ * arm_neon_rmsnorm_f32 (scripts/neon_rmsnorm.c:4-31). */
+Q6W_API int32_t q6w_rmsnorm(const float* x, const float* weight, float* out, int32_t n,
+                            int32_t length, float eps, q6w_stream_t stream);
+
+/* Decode attention of n independent sequences over their FP32 caches
+ * (torch_benchmark.py:113-119): for query head h (kv head h / groups_per_kv)
+ *   out[s,h,:] = softmax_t(q[s,h,:] . K[s,t,kv,:] / sqrt(head_dim)) V[s,t,kv,:]
+ * over t < lengths[s] (device int32, clamped to [0, max_len]; a length <= 0
+ * gives zeros).  queries/output: [n, kv_heads*groups_per_kv, head_dim];
+ * sequence s's keys/values start at keys/values + s*kv_seq_stride, laid out
+ * [max_len, kv_heads, head_dim] (one layer of the cache).  Replaces
+ * arm_neon_gqa_attention_f32 (scripts/neon_gqa_attention.c:11-95). */
+Q6W_API int32_t q6w_gqa_attention(const float* queries, const float* keys, const float* values,
+                                  float* output, const int32_t* lengths, int32_t n,
+                                  int32_t kv_heads, int32_t groups_per_kv, int32_t head_dim,
+                                  int32_t max_len, int64_t kv_seq_stride, q6w_stream_t stream);
+
+/* ---- model ------------------------------------------------------------- */
+
+typedef struct q6w_qmat {
+  const uint8_t* packed; /* [rows, cols*3/4] bytes */
+  const float* scales;   /* [rows] */
+  int32_t rows, cols;
+} q6w_qmat;
+
+typedef struct q6w_layer_weights {
+  q6w_qmat wq, wk, wv, wo, w1, w2, w3;
+  const float* attention_norm; /* [dim] */
+  const float* ffn_norm;       /* [dim] */
+} q6w_layer_weights;
+
+/* Model description: the manifest's model_args plus device pointers into the
+ * uploaded Q6W image (the file's bytes, unchanged).  `layers` is a HOST array
+ * of n_layers entries, copied by q6w_model_create. */
+typedef struct q6w_model_desc {
+  int32_t dim, n_layers, n_heads, n_kv_heads, vocab_size, hidden_dim, max_seq_len;
+  float norm_eps;
+  q6w_qmat tok_embeddings; /* [vocab, dim]; also the tied vocab head */
+  const float* norm;       /* final RMSNorm weight [dim] */
+  const float* rope_cos;   /* [max_seq_len, head_dim/2], host-built tables */
+  const float* rope_sin;
+  const q6w_layer_weights* layers; /* host */
+} q6w_model_desc;
+
+typedef struct q6w_model q6w_model;
+
+/* Validate a description (shapes, alignment, supported head_dim) and create
+ * a host-side handle.  Replaces CachedTransformer(args) +
+ * load_state_dict (benchmarks/torch_benchmark.py:57-77). */
+Q6W_API int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out);
+Q6W_API void q6w_model_destroy(q6w_model* model);
+
+/* Workspace (device scratch, caller-allocated, 256-byte aligned) needed to
+ * run up to max_seqs sequences per call. */
+Q6W_API size_t q6w_workspace_bytes(const q6w_model* model, int32_t max_seqs);
+
+/* KV cache: per sequence [n_layers, max_seq_len, n_kv_heads, head_dim] FP32,
+ * the layout of CachedTransformer.new_cache (torch_benchmark.py:87-94).
+ * Sequence s of a batch lives at k_cache + s * cache_seq_stride. */
+
+/* One cached step of a single sequence: token id and position are host
+ * values (validated here).  Writes the logits [vocab] row.
+ * Replaces CachedTransformer.step (benchmarks/torch_benchmark.py:96-125). */
+Q6W_API int32_t q6w_step(const q6w_model* model, int32_t token_id, int32_t position, float* k_cache,
+                 float* v_cache, float* logits, void* workspace, size_t workspace_bytes,
+                 q6w_stream_t stream);
+
+/* One cached step of n_seqs independent sequences: tokens[s] at
+ * positions[s] (device arrays).  logits is [n_seqs, vocab] or NULL; argmax
+ * (first maximum, as torch.argmax) is [n_seqs] or NULL.  Out-of-range
+ * tokens/positions are flagged on the device (see q6w_workspace_status) and
+ * that sequence's writes are skipped. */
+Q6W_API int32_t q6w_forward_batch(const q6w_model* model, int32_t n_seqs, const int32_t* tokens,
+                          const int32_t* positions, float* k_cache, float* v_cache,
+                          int64_t cache_seq_stride, float* logits, int32_t* argmax,
+                          void* workspace, size_t workspace_bytes, q6w_stream_t stream);
+
+/* Greedy generation of n_seqs independent requests, entirely on the device:
+ * token-by-token prefill of each (ragged) prompt, then greedy decode with
+ * the reference's stop contract -- stop ids masked to -inf while fewer than
+ * min_new_tokens tokens exist, first-maximum argmax, and a stop id picked
+ * afterwards ends the request without being appended
+ * (benchmarks/torch_benchmark.py:233-296 at temperature 0;
+ *  scripts/prepare_e2e.py:121-143;
+ *  rtl/autonomous/tinyllm_autonomous.cpp:1114-1150).
+ * One CUDA graph per step is replayed max_prompt_len + new_tokens - 1 times
+ * with no host synchronisation; the graph is cached in the model handle. */
+typedef struct q6w_greedy_args {
+  int32_t n_seqs;
+  const int32_t* prompts;     /* [n_seqs, prompt_stride] */
+  const int32_t* prompt_lens; /* [n_seqs], each in [1, max_prompt_len] */
+  int32_t prompt_stride;
+  int32_t max_prompt_len;     /* host value: max of prompt_lens */
+  int32_t new_tokens;         /* >= 1; max_prompt_len + new_tokens - 1 <= max_seq_len */
+  const int32_t* stop_ids;    /* host array of n_stop ids (copied), may be NULL */
+  int32_t n_stop;             /* 0..8 */
+  int32_t min_new_tokens;     /* 0..new_tokens */
+  int32_t* sampled;           /* [n_seqs, new_tokens]: every argmax pick, incl. a final stop id */
+  int32_t* n_sampled;         /* [n_seqs] */
+  int32_t* stop_reason;       /* [n_seqs]: the stop id that ended the request, or -1 */
+  float* k_cache;
+  float* v_cache;
+  int64_t cache_seq_stride;
+  float* step_logits;         /* [n_seqs, new_tokens, vocab] raw logits of each pick, or NULL */
+  void* prefill_event;        /* cudaEvent_t recorded after the first max_prompt_len steps, or NULL */
+} q6w_greedy_args;
+
+Q6W_API int32_t q6w_generate_greedy(q6w_model* model, const q6w_greedy_args* args, void* workspace,
+                            size_t workspace_bytes, q6w_stream_t stream);
+
+/* Synchronise `stream` and report device-side input errors recorded in the
+ * workspace since the last call (then clear them): Q6W_OK or Q6W_ERR_DEVICE. */
+Q6W_API int32_t q6w_workspace_status(void* workspace, q6w_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q6W_B200_H */

@@ -1,0 +1,188 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Run in a container that has the reference checkout (read-only) at
+``$Q6W_REFERENCE`` (default /root/reference):
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own ``quantization/q6w_format.py`` and
+``benchmarks/torch_benchmark.py`` and records what they produce:
+
+* ``codec.json``   -- packed bytes from the reference packer and the codes its
+  unpacker returns (including hand-made bytes holding the code 0x20 = -32,
+  which the reference decodes but never packs), plus ``quantize_rows``
+  outputs on seeded matrices with an all-zero row and exact .5 ties;
+* ``tiny_request.json`` -- the tiny synthetic model (dim 128, 5 layers, 8 q
+  heads, 4 kv heads, hidden 384, vocab 4096, context 256; weights N(0, 0.02)
+  from seed 1234, written by q6w_b200.format.write_synthetic and loaded by
+  the reference's ``load_dequantized_state``): a 20-token prompt drawn
+  U[3, 4095] from seed 7, 128 greedy tokens from the reference ``generate``,
+  the same request with a stop id and ``min_new_tokens`` through the
+  ``prepare_e2e`` loop, per-step top-1/top-2 margins, and the SHA-256 of the
+  binary so the writer + seed are pinned;
+* ``tiny_logits.npz`` -- reference logits of the last prompt step and the
+  first decode steps;
+* ``shipped_request.json`` -- the shipped QAT artifact on the standard
+  story-opening request (prompt ids from the shipped tokenizer), 128 greedy
+  tokens with min_new_tokens 4 and stop ids {BOS, EOS}.  The artifact itself
+  is not copied here.
+"""
+
+import hashlib
+import json
+import os
+import sys
+import tempfile
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+REF = Path(os.environ.get("Q6W_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(REPO / "tinyllm-pynq-z2_b200"))
+sys.path.insert(0, str(REF / "quantization"))
+sys.path.insert(0, str(REF / "benchmarks"))
+
+import q6w_format as ref_fmt  # noqa: E402
+import torch_benchmark as ref_tb  # noqa: E402
+from q6w_b200 import format as fmt  # noqa: E402
+
+DEFAULTS = {"hidden_dim": None, "multiple_of": 256, "norm_eps": 1e-5, "n_kv_heads": None, "max_seq_len": 2048,
+            "dropout": 0.0}
+TINY_SEED = 1234
+PROMPT_SEED = 7
+
+
+def codec_vectors():
+    rng = np.random.default_rng(20261201)
+    out = {"pack": [], "unpack_only": [], "quantize": []}
+    for rows, cols in ((1, 4), (3, 16), (4, 128), (2, 352)):
+        q = rng.integers(-31, 32, size=(rows, cols))
+        packed = ref_fmt.pack_signed_int6(q)
+        back = ref_fmt.unpack_signed_int6(packed, rows, cols)
+        out["pack"].append({"rows": rows, "cols": cols, "codes": q.tolist(), "packed_hex": packed.hex(),
+                            "unpacked": back.tolist()})
+    # every 6-bit pattern, 0x20 (-32) included, from raw bytes
+    fields = np.arange(64, dtype=np.int64).reshape(16, 4)
+    word = fields[:, 0] | (fields[:, 1] << 6) | (fields[:, 2] << 12) | (fields[:, 3] << 18)
+    raw = np.stack([word & 255, (word >> 8) & 255, (word >> 16) & 255], axis=1).astype(np.uint8).tobytes()
+    out["unpack_only"].append({"rows": 1, "cols": 64, "packed_hex": raw.hex(),
+                               "unpacked": ref_fmt.unpack_signed_int6(raw, 1, 64).tolist()})
+    raw2 = bytes(rng.integers(0, 256, size=3 * 8 * 12, dtype=np.uint8))
+    out["unpack_only"].append({"rows": 8, "cols": 48, "packed_hex": raw2.hex(),
+                               "unpacked": ref_fmt.unpack_signed_int6(raw2, 8, 48).tolist()})
+    g = torch.Generator().manual_seed(99)
+    w = torch.empty(6, 32).normal_(0, 0.02, generator=g)
+    w[2] = 0.0
+    w[3] = torch.tensor([0.5, -1.5, 2.5, 31.0] * 8) / 31.0 * 0.1  # exact-ish ties after scaling
+    w[4, :4] = torch.tensor([1.0, -1.0, 0.5, -0.5])
+    q, s, stats = ref_fmt.quantize_rows(w)
+    out["quantize"].append({"weights": w.tolist(), "q": q.tolist(), "scales": s.astype(np.float32).tolist(),
+                            "stats": stats})
+    return out
+
+
+def load_reference_model(bin_path, manifest_path, max_seq_len=None):
+    manifest = json.loads(Path(manifest_path).read_text())
+    shapes = fmt._model_shapes(manifest["model_args"])
+    template = {k: torch.zeros(v) for k, v in shapes.items()}
+    template["output.weight"] = template["tok_embeddings.weight"]
+    state, manifest = ref_fmt.load_dequantized_state(bin_path, manifest_path, template)
+    args = SimpleNamespace(**{**DEFAULTS, **manifest["model_args"]})
+    if max_seq_len:
+        args.max_seq_len = max_seq_len
+    model = ref_tb.CachedTransformer(args).eval()
+    model.load_state_dict(state, strict=True)
+    return model, manifest
+
+
+def greedy_with_stops(model, prompt, new_tokens, stop_ids, min_new):
+    """scripts/prepare_e2e.py:120-143, verbatim in behaviour."""
+    k, v = model.new_cache(torch.device("cpu"))
+    rows, sampled, generated, margins = [], [], [], []
+    stopped_on = None
+    with torch.inference_mode():
+        for pos, tok in enumerate(prompt):
+            logits = model.step(tok, pos, k, v)
+        for index in range(new_tokens):
+            rows.append(logits.clone())
+            scores = logits.clone()
+            if index < min_new:
+                for t in stop_ids:
+                    scores[t] = -float("inf")
+            t = int(torch.argmax(scores).item())
+            top2 = torch.topk(scores, 2).values
+            margins.append(float(top2[0] - top2[1]))
+            sampled.append(t)
+            if index >= min_new and t in stop_ids:
+                stopped_on = t
+                break
+            generated.append(t)
+            if index + 1 < new_tokens:
+                logits = model.step(t, len(prompt) + index, k, v)
+    return {"sampled": sampled, "generated": generated, "stopped_on": stopped_on, "margins": margins,
+            "logits": torch.stack(rows)}
+
+
+def tiny_request(tmp):
+    b, m = tmp / "tiny.bin", tmp / "tiny.json"
+    fmt.write_synthetic(fmt.TINY_ARGS, TINY_SEED, b, m)
+    sha = hashlib.sha256(b.read_bytes()).hexdigest()
+    model, manifest = load_reference_model(b, m)
+    prompt = torch.randint(3, 4096, (20,), generator=torch.Generator().manual_seed(PROMPT_SEED)).tolist()
+    with torch.inference_mode():
+        gen, _, _, stopped, reason = ref_tb.generate(model, prompt, 128, torch.device("cpu"))
+    plain = greedy_with_stops(model, prompt, 128, [], 0)
+    assert plain["generated"] == gen
+    # a stop id the model really emits, so masking and stopping both engage
+    distinct = [t for t in dict.fromkeys(gen)]
+    stop_id = distinct[1] if len(distinct) > 1 else distinct[0]
+    min_new = 3
+    stop_run = greedy_with_stops(model, prompt, 128, [stop_id], min_new)
+    logits = {"prompt_last": plain["logits"][0].numpy(), "decode_1_4": plain["logits"][1:5].numpy(),
+              "stop_run_first": stop_run["logits"][0].numpy()}
+    doc = {
+        "model_args": manifest["model_args"], "seed": TINY_SEED, "binary_sha256": sha,
+        "binary_bytes": b.stat().st_size, "prompt_seed": PROMPT_SEED, "prompt": prompt, "new_tokens": 128,
+        "generated": gen, "stopped": stopped, "margins": plain["margins"],
+        "stop_case": {"stop_ids": [stop_id], "min_new_tokens": min_new, "sampled": stop_run["sampled"],
+                      "generated": stop_run["generated"], "stopped_on": stop_run["stopped_on"]},
+        "torch": torch.__version__,
+    }
+    return doc, logits
+
+
+def shipped_request():
+    art = REF / "quantization" / "artifacts"
+    b, m = art / "tinyllamas_zh_story_q6w_qat_lr1e6.bin", art / "tinyllamas_zh_story_q6w_qat_lr1e6.json"
+    manifest = json.loads(m.read_text())
+    model, manifest = load_reference_model(b, m, manifest["model_args"]["max_seq_len"])
+    from sentencepiece import SentencePieceProcessor
+
+    sp = SentencePieceProcessor(model_file=str(REF / "tok4096.model"))
+    text = "故事开头：{}\n续写：".format("从前，有一只叫小白的兔子。")
+    prompt = [int(sp.bos_id())] + [int(t) for t in sp.encode(text)]
+    stop_ids = sorted({int(sp.bos_id()), int(sp.eos_id())})
+    run = greedy_with_stops(model, prompt, 128, stop_ids, 4)
+    return {"binary_file": b.name, "binary_sha256": manifest["binary_sha256"], "model_args": manifest["model_args"],
+            "prompt": prompt, "new_tokens": 128, "min_new_tokens": 4, "stop_ids": stop_ids,
+            "sampled": run["sampled"], "generated": run["generated"], "stopped_on": run["stopped_on"],
+            "margins": run["margins"], "torch": torch.__version__}
+
+
+def main():
+    torch.set_num_threads(1)
+    (HERE / "codec.json").write_text(json.dumps(codec_vectors(), indent=1) + "\n")
+    with tempfile.TemporaryDirectory() as d:
+        doc, logits = tiny_request(Path(d))
+    (HERE / "tiny_request.json").write_text(json.dumps(doc, indent=1) + "\n")
+    np.savez_compressed(HERE / "tiny_logits.npz", **logits)
+    (HERE / "shipped_request.json").write_text(json.dumps(shipped_request(), ensure_ascii=False, indent=1) + "\n")
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

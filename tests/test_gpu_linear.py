@@ -1,0 +1,94 @@
+"""GPU: the Q6W linear (isolated sweep on the tiny model's shapes) against an
+FP64 dequant-then-matmul reference and torch FP32.
+
+Tolerance (FP32 path): |y - y64| <= 1e-5 * sum_k |w_k x_k| + 1e-30 per
+element, i.e. FP32 summation error relative to the magnitude of the terms.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec
+from q6w_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(128, 128), (64, 128), (384, 128), (128, 384), (4096, 128)]
+BATCHES = [1, 8, 64, 512, 4096]
+REL = 1e-5
+
+
+def make(rows, cols, n, seed):
+    rng = np.random.default_rng(seed)
+    q = rng.integers(-32, 32, size=(rows, cols))
+    s = rng.uniform(0.001, 0.05, size=rows).astype(np.float32)
+    x = rng.standard_normal((n, cols)).astype(np.float32)
+    packed = torch.frombuffer(bytearray(codec.pack_int6(q, allow_minus32=True)), dtype=torch.uint8).cuda()
+    return q, s, x, packed
+
+
+def check(y, q, s, x):
+    w = codec.dequantize(q, s).astype(np.float64)
+    y64 = x.astype(np.float64) @ w.T
+    mag = np.abs(x.astype(np.float64)) @ np.abs(w).T
+    err = np.abs(y.astype(np.float64) - y64)
+    assert (err <= REL * mag + 1e-30).all(), float((err / (mag + 1e-30)).max())
+
+
+@pytest.mark.parametrize("rows,cols", SHAPES)
+@pytest.mark.parametrize("n", BATCHES)
+def test_linear_sweep(rows, cols, n):
+    q, s, x, packed = make(rows, cols, n, rows * 7 + cols * 3 + n)
+    y = ops.q6w_linear(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    check(y, q, s, x)
+    ref32 = torch.from_numpy(x) @ torch.from_numpy(codec.dequantize(q, s)).T
+    assert np.abs(y - ref32.numpy()).max() <= 1e-4
+
+
+@pytest.mark.parametrize("rows,cols,n", [(63, 128, 3), (6, 20, 9), (10, 36, 1), (2, 4, 1), (4096, 128, 2)])
+def test_linear_general_shapes(rows, cols, n):
+    q, s, x, packed = make(rows, cols, n, 11 + rows + cols + n)
+    y = ops.q6w_linear(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols).cpu().numpy()
+    check(y, q, s, x)
+
+
+def test_linear_unaligned_x_uses_general_path():
+    q, s, x, packed = make(64, 128, 4, 5)
+    buf = torch.zeros(4 * 128 + 1, device="cuda")
+    xv = buf[1:].view(4, 128)
+    xv.copy_(torch.from_numpy(x))
+    y = ops.q6w_linear(xv, packed, torch.from_numpy(s).cuda(), 64, 128).cpu().numpy()
+    check(y, q, s, x)
+
+
+@pytest.mark.parametrize("rows,cols,n", [(4096, 128, 1), (4096, 128, 3), (4096, 128, 300), (32000, 256, 2)])
+def test_linear_argmax(rows, cols, n):
+    q, s, x, packed = make(rows, cols, n, 99 + n)
+    am, lg = ops.linear_argmax(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols, True)
+    lg = lg.cpu().numpy()
+    check(lg, q, s, x)
+    assert np.array_equal(am.cpu().numpy(), lg.argmax(axis=1))  # first maximum of the device logits
+
+
+def test_linear_argmax_ties_pick_first():
+    rows, cols = 64, 16
+    q = np.zeros((rows, cols), dtype=np.int64)
+    q[[5, 9, 40], 0] = 7  # three equal maxima
+    s = np.full(rows, 0.01, dtype=np.float32)
+    packed = torch.frombuffer(bytearray(codec.pack_int6(q)), dtype=torch.uint8).cuda()
+    x = torch.zeros(2, cols, device="cuda")
+    x[:, 0] = 1.0
+    am, _ = ops.linear_argmax(x, packed, torch.from_numpy(s).cuda(), rows, cols)
+    assert am.cpu().tolist() == [5, 5]
+
+
+def test_rmsnorm_matches_reference_formula():
+    torch.manual_seed(0)
+    x = torch.randn(37, 128)
+    w = torch.rand(128) + 0.5
+    got = ops.rmsnorm(x.cuda(), w.cuda(), 1e-5).cpu()
+    want = (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-5)) * w
+    assert (got - want).abs().max() <= 2e-6

@@ -1,0 +1,233 @@
+"""GPU: the cached step, the batched step and the device greedy loop against
+the oracle (and through it, the reference's golden requests).
+
+Tolerances: logits within 2e-4 absolute of the oracle (the reference's own
+cached-vs-uncached check, benchmarks/torch_benchmark.py:316); greedy token
+ids and per-step argmaxes exactly equal on the golden requests; batched
+device streams verified by teacher forcing (every pick is the oracle's
+argmax, or an FP32 near-tie within 1e-4 of the oracle's maximum, and the
+stop/length contract holds).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, small_model_files
+from oracle.model import BatchScorer, OracleModel, greedy_request
+from q6w_b200 import format as fmt
+from q6w_b200 import generate, ops
+from q6w_b200.model import Q6WCudaTransformer
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-4
+
+
+@pytest.fixture(scope="module")
+def tiny(tiny_files):
+    return Q6WCudaTransformer.from_q6w(*tiny_files), OracleModel.from_q6w(*tiny_files)
+
+
+def test_step_logits_match_oracle(tiny, golden_tiny):
+    cuda, orc = tiny
+    k, v = cuda.new_cache()
+    ko, vo = orc.new_cache()
+    worst = 0.0
+    with torch.inference_mode():
+        for pos, tok in enumerate(golden_tiny["prompt"]):
+            a = cuda.step(tok, pos, k, v).cpu()
+            b = orc.step(tok, pos, ko, vo)
+            worst = max(worst, float((a - b).abs().max()))
+    assert worst <= LOGIT_TOL
+    ref = np.load(GOLDEN / "tiny_logits.npz")["prompt_last"]
+    assert np.abs(a.numpy() - ref).max() <= LOGIT_TOL
+    # cache contents: rotated keys and raw values of every prompt position
+    P = len(golden_tiny["prompt"])
+    assert (k[:, :P].cpu() - ko[:, :P]).abs().max() <= 1e-4
+    assert (v[:, :P].cpu() - vo[:, :P]).abs().max() <= 1e-4
+
+
+def test_drop_in_host_loop_is_token_exact(tiny, golden_tiny):
+    """The oracle's own greedy loop driving Q6WCudaTransformer.step."""
+    cuda, _ = tiny
+    out = greedy_request(cuda, golden_tiny["prompt"], golden_tiny["new_tokens"])
+    assert out["generated"] == golden_tiny["generated"]
+
+
+def test_generate_device_loop_is_token_exact(tiny, golden_tiny):
+    cuda, _ = tiny
+    gen, pre_s, dec_s, stopped, reason = generate(cuda, golden_tiny["prompt"], golden_tiny["new_tokens"], cuda.device)
+    assert gen == golden_tiny["generated"] and not stopped and reason is None
+    assert pre_s > 0 and dec_s > 0
+
+
+def test_generate_stop_contract(tiny, golden_tiny):
+    cuda, _ = tiny
+    case = golden_tiny["stop_case"]
+    res = cuda.generate_greedy([golden_tiny["prompt"]], golden_tiny["new_tokens"], case["stop_ids"],
+                               case["min_new_tokens"], keep_logits=True)
+    assert res.sampled[0] == case["sampled"]
+    assert res.generated[0] == case["generated"]
+    assert res.stop_reason[0] == case["stopped_on"]
+    first = np.load(GOLDEN / "tiny_logits.npz")["stop_run_first"]
+    assert np.abs(res.logits[0, 0].cpu().numpy() - first).max() <= LOGIT_TOL
+
+
+def test_generate_matches_reference_signature_errors(tiny):
+    cuda, _ = tiny
+    with pytest.raises(ValueError):
+        generate(cuda, [5, 6], 4, cuda.device, min_new_tokens=5)
+    with pytest.raises(NotImplementedError):
+        generate(cuda, [5, 6], 4, cuda.device, temperature=0.7)
+    with pytest.raises(ValueError):
+        cuda.generate_greedy([[1] * 250], 10)  # exceeds the 256-position context
+
+
+def test_step_range_errors(tiny):
+    cuda, _ = tiny
+    k, v = cuda.new_cache()
+    with pytest.raises(IndexError):
+        cuda.step(1, cuda.args.max_seq_len, k, v)
+    with pytest.raises(IndexError):
+        cuda.step(cuda.args.vocab_size, 0, k, v)
+
+
+def test_forward_batch_bad_token_flagged(tiny):
+    cuda, _ = tiny
+    k, v = cuda.new_batch_cache(3)
+    toks = torch.tensor([5, 99999, 7], dtype=torch.int32, device="cuda")
+    pos = torch.zeros(3, dtype=torch.int32, device="cuda")
+    lg, _ = cuda.forward_batch(toks, pos, k, v)
+    ws, _ = cuda.workspace(3)
+    from q6w_b200 import Q6WError
+
+    with pytest.raises(Q6WError):
+        cuda.check_device_status(ws)
+    cuda.check_device_status(ws)  # cleared
+
+
+@pytest.mark.parametrize("n", [1, 3, 8, 37, 200])
+def test_forward_batch_matches_oracle(tiny, n):
+    cuda, orc = tiny
+    g = torch.Generator().manual_seed(n)
+    T = 6
+    toks = torch.randint(0, 4096, (T, n), generator=g)
+    k, v = cuda.new_batch_cache(n)
+    for t in range(T):
+        lg, am = cuda.forward_batch(toks[t].int().cuda(), torch.full((n,), t, dtype=torch.int32).cuda(), k, v,
+                                    argmax=True)
+    # ragged positions: re-run some sequences at an earlier position
+    pos = torch.tensor([T if i % 3 else T - 3 for i in range(n)], dtype=torch.int32)
+    last = torch.randint(0, 4096, (n,), generator=g)
+    lg, am = cuda.forward_batch(last.int().cuda(), pos.cuda(), k, v, argmax=True)
+    lg = lg.cpu()
+    assert torch.equal(am.cpu().long(), lg.argmax(dim=1))
+    for i in range(0, n, max(1, n // 12)):
+        ko, vo = orc.new_cache()
+        with torch.inference_mode():
+            for t in range(T):
+                orc.step(int(toks[t, i]), t, ko, vo)
+            want = orc.step(int(last[i]), int(pos[i]), ko, vo)
+        assert float((lg[i] - want).abs().max()) <= LOGIT_TOL, i
+
+
+def _ragged_prompts(n, seed, lo=1, hi=40):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(lo, hi + 1, (n,), generator=g).tolist()
+    return [torch.randint(3, 4096, (L,), generator=g).tolist() for L in lens]
+
+
+@pytest.mark.parametrize("n,new", [(64, 24), (600, 12)])
+def test_generate_batch_teacher_forced(tiny, n, new):
+    cuda, orc = tiny
+    prompts = _ragged_prompts(n, n)
+    res = cuda.generate_greedy(prompts, new)
+    idx = list(range(0, n, max(1, n // 64)))
+    summary = BatchScorer(orc).verify_greedy([prompts[i] for i in idx], [res.sampled[i] for i in idx], new)
+    assert summary["failures"] == [], summary["failures"][:5]
+    assert summary["exact"] >= 0.99 * summary["picks"]
+    assert all(len(s) == new for s in res.sampled)
+
+
+def test_generate_batch_with_stops(tiny, golden_tiny):
+    cuda, orc = tiny
+    case = golden_tiny["stop_case"]
+    prompts = _ragged_prompts(16, 3) + [golden_tiny["prompt"]]
+    res = cuda.generate_greedy(prompts, 60, case["stop_ids"], case["min_new_tokens"])
+    assert res.sampled[-1] == case["sampled"][:60] or res.sampled[-1] == case["sampled"]
+    summary = BatchScorer(orc).verify_greedy(prompts, res.sampled, 60, case["stop_ids"], case["min_new_tokens"])
+    assert summary["failures"] == []
+
+
+@pytest.fixture(scope="module")
+def shipped_shape(tmp_path_factory):
+    """Synthetic model with the shipped artifact's shapes: 4 q heads, 2 kv heads,
+    head_dim 32, hidden 352 (from the multiple_of rule), context 512."""
+    args = {"dim": 128, "n_layers": 5, "n_heads": 4, "n_kv_heads": 2, "vocab_size": 4096, "multiple_of": 32,
+            "max_seq_len": 512, "dropout": 0.0}
+    b, m = small_model_files(tmp_path_factory, args, 77, "shipshape")
+    return Q6WCudaTransformer.from_q6w(b, m), OracleModel.from_q6w(b, m)
+
+
+def test_shipped_shapes_parity(shipped_shape):
+    cuda, orc = shipped_shape
+    assert cuda.hidden_dim == 352
+    prompt = _ragged_prompts(1, 11, 20, 20)[0]
+    want = greedy_request(orc, prompt, 48)
+    res = cuda.generate_greedy([prompt], 48)
+    assert res.generated[0] == want["generated"]
+    k, v = cuda.new_cache()
+    ko, vo = orc.new_cache()
+    for p, t in enumerate(prompt[:5]):
+        a = cuda.step(t, p, k, v).cpu()
+        b = orc.step(t, p, ko, vo)
+    assert float((a - b).abs().max()) <= LOGIT_TOL
+
+
+def test_scaled_shapes_parity(tmp_path_factory):
+    """The 1.1B-shape config's matrices (dim 2048, 32 heads, 4 kv heads,
+    hidden 5632, vocab 32000) with one layer, against the oracle."""
+    args = dict(fmt.SCALED_ARGS, n_layers=1, max_seq_len=32)
+    b, m = small_model_files(tmp_path_factory, args, 5, "scaled1")
+    cuda, orc = Q6WCudaTransformer.from_q6w(b, m), OracleModel.from_q6w(b, m)
+    k, v = cuda.new_cache()
+    ko, vo = orc.new_cache()
+    prompt = [17, 2500, 31999, 4, 1234]
+    for p, t in enumerate(prompt):
+        a = cuda.step(t, p, k, v).cpu()
+        with torch.inference_mode():
+            bb = orc.step(t, p, ko, vo)
+        assert float((a - bb).abs().max()) <= LOGIT_TOL
+    # batched path on the same model (gemv n<=8 and tiled n>8 kernels)
+    for n in (4, 20):
+        kb, vb = cuda.new_batch_cache(n)
+        for p, t in enumerate(prompt):
+            lg, _ = cuda.forward_batch(torch.full((n,), t, dtype=torch.int32).cuda(),
+                                       torch.full((n,), p, dtype=torch.int32).cuda(), kb, vb)
+        assert float((lg.cpu() - bb).abs().max()) <= LOGIT_TOL
+
+
+def test_shipped_artifact_request(shipped_files_env, golden_shipped):
+    cuda = Q6WCudaTransformer.from_q6w(*shipped_files_env)
+    g = golden_shipped
+    res = cuda.generate_greedy([g["prompt"]], g["new_tokens"], g["stop_ids"], g["min_new_tokens"])
+    assert res.sampled[0] == g["sampled"]
+    assert res.generated[0] == g["generated"]
+
+
+def test_gqa_attention_op(tiny):
+    """The public attention op against torch's softmax attention."""
+    torch.manual_seed(3)
+    n, L, KV, rep, hd = 5, 40, 4, 2, 16
+    q = torch.randn(n, KV * rep, hd)
+    kk = torch.randn(n, L, KV, hd)
+    vv = torch.randn(n, L, KV, hd)
+    lens = torch.tensor([1, 7, 40, 33, 12], dtype=torch.int32)
+    out = ops.gqa_attention(q.cuda(), kk.cuda(), vv.cuda(), lens.cuda(), rep).cpu()
+    for i in range(n):
+        T = int(lens[i])
+        ks = kk[i, :T].permute(1, 0, 2).repeat_interleave(rep, 0)
+        vs = vv[i, :T].permute(1, 0, 2).repeat_interleave(rep, 0)
+        w = torch.softmax((q[i].unsqueeze(1) @ ks.transpose(1, 2)) / hd ** 0.5, -1)
+        want = (w @ vs).squeeze(1)
+        assert (out[i] - want).abs().max() <= 1e-5

@@ -1,0 +1,89 @@
+"""CPU: the oracle (and the product's host codec) pinned to the reference's
+own outputs recorded in tests/golden/ by make_golden.py."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec
+from oracle.model import OracleModel, greedy_request
+from q6w_b200 import format as fmt
+
+
+def test_pack_matches_reference_bytes(golden_codec):
+    for case in golden_codec["pack"]:
+        q = np.array(case["codes"])
+        assert codec.pack_int6(q).hex() == case["packed_hex"]
+        assert fmt.pack_signed_int6(q).hex() == case["packed_hex"]
+
+
+def test_unpack_matches_reference(golden_codec):
+    for case in golden_codec["pack"] + golden_codec["unpack_only"]:
+        got = codec.unpack_int6(bytes.fromhex(case["packed_hex"]), case["rows"], case["cols"])
+        assert got.tolist() == case["unpacked"]
+
+
+def test_unpack_covers_all_codes(golden_codec):
+    case = golden_codec["unpack_only"][0]
+    got = codec.unpack_int6(bytes.fromhex(case["packed_hex"]), 1, 64)
+    assert sorted(got[0].tolist()) == list(range(-32, 32))
+
+
+def test_quantize_rows_matches_reference(golden_codec):
+    for case in golden_codec["quantize"]:
+        w = torch.tensor(case["weights"], dtype=torch.float32)
+        q, s = codec.quantize_rows(w)
+        assert q.tolist() == case["q"]
+        assert np.array_equal(s, np.array(case["scales"], dtype=np.float32))
+        q2, s2, stats = fmt.quantize_rows(w)
+        assert q2.tolist() == case["q"] and np.array_equal(s2, s)
+        assert stats["max_abs_error"] == pytest.approx(case["stats"]["max_abs_error"], rel=1e-6)
+
+
+def test_oracle_tiny_request_tokens(tiny_files, golden_tiny):
+    m = OracleModel.from_q6w(*tiny_files)
+    out = greedy_request(m, golden_tiny["prompt"], golden_tiny["new_tokens"])
+    assert out["generated"] == golden_tiny["generated"]
+    assert np.allclose(out["margins"], golden_tiny["margins"], atol=1e-6)
+
+
+def test_oracle_tiny_logits(tiny_files, golden_tiny):
+    ref = np.load(__import__("conftest").GOLDEN / "tiny_logits.npz")
+    m = OracleModel.from_q6w(*tiny_files)
+    out = greedy_request(m, golden_tiny["prompt"], 5, keep_logits=True)
+    got = out["logits"].numpy()
+    # bitwise on the machine that made the fixture; FP32-rounding close elsewhere
+    assert np.abs(got[0] - ref["prompt_last"]).max() <= 1e-5
+    assert np.abs(got[1:5] - ref["decode_1_4"]).max() <= 1e-5
+
+
+def test_oracle_stop_contract(tiny_files, golden_tiny):
+    case = golden_tiny["stop_case"]
+    m = OracleModel.from_q6w(*tiny_files)
+    out = greedy_request(m, golden_tiny["prompt"], golden_tiny["new_tokens"], case["stop_ids"], case["min_new_tokens"])
+    assert out["sampled"] == case["sampled"]
+    assert out["generated"] == case["generated"]
+    assert out["stopped_on"] == case["stopped_on"]
+
+
+def test_oracle_shipped_request(shipped_files, golden_shipped):
+    m = OracleModel.from_q6w(*shipped_files)
+    g = golden_shipped
+    out = greedy_request(m, g["prompt"], g["new_tokens"], g["stop_ids"], g["min_new_tokens"])
+    assert out["sampled"] == g["sampled"]
+    assert out["generated"] == g["generated"]
+
+
+def test_batch_scorer_agrees_with_step(tiny_files, golden_tiny):
+    from oracle.model import BatchScorer
+
+    m = OracleModel.from_q6w(*tiny_files)
+    sc = BatchScorer(m)
+    prompts = [golden_tiny["prompt"], golden_tiny["prompt"][:7]]
+    outs = [greedy_request(m, p, 12) for p in prompts]
+    summary = sc.verify_greedy(prompts, [o["sampled"] for o in outs], 12)
+    assert summary["failures"] == [] and summary["picks"] == 24
+    # a planted wrong pick is caught
+    bad = [list(o["sampled"]) for o in outs]
+    bad[1][3] = (bad[1][3] + 1) % 4096
+    assert sc.verify_greedy(prompts, bad, 12)["failures"]

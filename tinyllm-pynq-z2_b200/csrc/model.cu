@@ -1,0 +1,748 @@
+// Cached decode step of the Q6W transformer on sm_100a, and the device-resident
+// greedy generation loop.
+//
+// One step for n sequences (each at its own position) is:
+//   embed  -> x = dequant(E[token])                              (a4)
+//   per layer l:
+//     qkv    RMSNorm prologue, [wq|wk|wv] linear, RoPE, K/V cache write   (a5, a3, a6, a7)
+//     attn   softmax(q K^T / sqrt(hd)) V over positions 0..pos, GQA       (a7)
+//     wo     linear + residual add                                       (a3, a9)
+//     ffn1   RMSNorm prologue, W1 and W3 together, silu(a) * b            (a5, a8)
+//     w2     linear + residual add                                       (a8, a9)
+//   vocab  RMSNorm prologue, tied-embedding linear, logits and
+//          first-maximum argmax (with stop-id masking)               (a10)
+// mirroring CachedTransformer.step (benchmarks/torch_benchmark.py:96-125).
+// The greedy loop appends an `advance` kernel that applies the stop contract
+// of torch_benchmark.py:272-293 / scripts/prepare_e2e.py:129-143 per
+// sequence and feeds the next token; the whole step is captured once into a
+// CUDA graph and replayed, so the host never synchronises inside a request.
+#include <math.h>
+#include <string.h>
+
+#include <new>
+#include <vector>
+
+#include "linear.cuh"
+
+namespace q6w {
+
+struct Work {
+  float* x;
+  float* qb;
+  float* att;
+  float* hb;
+  unsigned long long* keys;
+  int32_t* tok;
+  int32_t* pos;
+  int32_t* plen;
+  int32_t* gen;
+  int32_t* flags;
+  int32_t* err;
+};
+
+struct GraphKey {
+  q6w_greedy_args a;
+  int32_t stop[kMaxStop];
+  void* ws;
+};
+
+}  // namespace q6w
+
+struct q6w_model {
+  q6w_model_desc d;
+  std::vector<q6w_layer_weights> layers;
+  int32_t hd, kv_rows;
+  float denom;
+  int device;
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  q6w::GraphKey key;
+  bool have_key = false;
+};
+
+namespace q6w {
+
+static size_t carve(char*& p, size_t bytes) {
+  size_t off = (size_t)p;
+  p += (bytes + 255) & ~(size_t)255;
+  return off;
+}
+
+static size_t layout(const q6w_model* M, int N, char* base, Work* w) {
+  const auto& d = M->d;
+  char* p = base;
+  Work t;
+  t.err = (int32_t*)carve(p, 4);  // first: q6w_workspace_status reads offset 0
+  t.x = (float*)carve(p, sizeof(float) * (size_t)N * d.dim);
+  t.qb = (float*)carve(p, sizeof(float) * (size_t)N * d.dim);
+  t.att = (float*)carve(p, sizeof(float) * (size_t)N * d.dim);
+  t.hb = (float*)carve(p, sizeof(float) * (size_t)N * d.hidden_dim);
+  t.keys = (unsigned long long*)carve(p, sizeof(unsigned long long) * (size_t)N);
+  t.tok = (int32_t*)carve(p, 4 * (size_t)N);
+  t.pos = (int32_t*)carve(p, 4 * (size_t)N);
+  t.plen = (int32_t*)carve(p, 4 * (size_t)N);
+  t.gen = (int32_t*)carve(p, 4 * (size_t)N);
+  t.flags = (int32_t*)carve(p, 4 * (size_t)N);
+  if (w) *w = t;
+  return (size_t)(p - base);
+}
+
+// ---- small kernels -----------------------------------------------------------
+
+__global__ void init_batch_kernel(int n, const int32_t* __restrict__ tokens,
+                                  const int32_t* __restrict__ positions, int32_t tok_scalar,
+                                  int32_t pos_scalar, Work w) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n; b += gridDim.x * blockDim.x) {
+    w.tok[b] = tokens ? tokens[b] : tok_scalar;
+    w.pos[b] = positions ? positions[b] : pos_scalar;
+    w.plen[b] = 0;
+    w.gen[b] = 0;
+    w.flags[b] = 0;
+    w.keys[b] = 0ull;
+  }
+}
+
+__global__ void init_greedy_kernel(int n, const int32_t* __restrict__ prompts,
+                                   const int32_t* __restrict__ lens, int32_t stride,
+                                   int32_t max_len, Work w, int32_t* n_sampled,
+                                   int32_t* stop_reason) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n; b += gridDim.x * blockDim.x) {
+    const int32_t L = lens[b];
+    const bool ok = L >= 1 && L <= max_len;
+    w.tok[b] = ok ? prompts[(int64_t)b * stride] : 0;
+    w.pos[b] = 0;
+    w.plen[b] = ok ? L : 1;
+    w.gen[b] = 0;
+    w.flags[b] = ok ? 0 : (SEQ_DONE | SEQ_INVALID);
+    w.keys[b] = 0ull;
+    n_sampled[b] = 0;
+    stop_reason[b] = -1;
+    if (!ok) atomicOr(w.err, 1);
+  }
+}
+
+// x[b] = float(E[token]) * scale[token]; also validates token/position.
+__global__ void embed_kernel(const uint8_t* __restrict__ E, const float* __restrict__ Es, int dim,
+                             int vocab, int max_seq, int n, Work w) {
+  const int groups = dim >> 2;
+  for (int b = blockIdx.x; b < n; b += gridDim.x) {
+    const int t = w.tok[b], p = w.pos[b];
+    const bool ok = t >= 0 && t < vocab && p >= 0 && p < max_seq;
+    if (threadIdx.x == 0) {
+      const int f = w.flags[b];
+      w.flags[b] = ok ? (f & ~SEQ_INVALID) : (f | SEQ_INVALID);
+      if (!ok && !(f & SEQ_DONE)) atomicOr(w.err, 1);
+    }
+    float* xr = w.x + (int64_t)b * dim;
+    if (!ok) {
+      for (int c = threadIdx.x; c < dim; c += blockDim.x) xr[c] = 0.0f;
+      continue;
+    }
+    const uint8_t* row = E + (int64_t)t * groups * 3;
+    const float s = __ldg(Es + t);
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+      const uint32_t v = load_group(row + 3 * g);
+      reinterpret_cast<float4*>(xr)[g] =
+          make_float4(__fmul_rn((float)group_code(v, 0), s), __fmul_rn((float)group_code(v, 1), s),
+                      __fmul_rn((float)group_code(v, 2), s), __fmul_rn((float)group_code(v, 3), s));
+    }
+  }
+}
+
+// Decode attention over the FP32 cache (torch_benchmark.py:113-119).
+// One warp per (sequence, query head); G lanes share one cached position
+// (16 head dims per lane), 32/G positions per pass.  Pass 1 writes the
+// scaled scores to shared memory, pass 2 the max-subtracted exponentials,
+// pass 3 accumulates the normalised weights times V.
+template <int G>
+__global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb, int ldq,
+                                                   const float* __restrict__ kc,
+                                                   const float* __restrict__ vc, int64_t cstride,
+                                                   int64_t layer_off, const int32_t* __restrict__ len,
+                                                   int len_add, const int32_t* __restrict__ flags,
+                                                   float* __restrict__ out, int ldo, int H, int KV,
+                                                   int S, float denom) {
+  extern __shared__ float sc[];
+  constexpr int P = 32 / G;
+  constexpr int HD = 16 * G;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x, h = blockIdx.y * (blockDim.x >> 5) + warp;
+  if (h >= H) return;
+  const int slot = lane / G, part = lane % G;
+  float* o = out + (int64_t)b * ldo + h * HD + 16 * part;
+  int T = len[b] + len_add;
+  T = T > S ? S : T;
+  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
+    if (slot == 0)
+      for (int i = 0; i < 16; ++i) o[i] = 0.0f;
+    return;
+  }
+  const int g = h / (H / KV);
+  const int kvr = KV * HD;
+  const float* kb = kc + b * cstride + layer_off + g * HD + 16 * part;
+  const float* vb = vc + b * cstride + layer_off + g * HD + 16 * part;
+  float q[16];
+  {
+    const float4* qp = reinterpret_cast<const float4*>(qb + (int64_t)b * ldq + h * HD + 16 * part);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 v = qp[j];
+      q[4 * j] = v.x; q[4 * j + 1] = v.y; q[4 * j + 2] = v.z; q[4 * j + 3] = v.w;
+    }
+  }
+  float* s = sc + warp * S;
+  float mx = -INFINITY;
+  for (int t0 = 0; t0 < T; t0 += P) {
+    const int t = t0 + slot;
+    float d = 0.0f;
+    if (t < T) {
+      const float4* kp = reinterpret_cast<const float4*>(kb + (int64_t)t * kvr);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 k4 = kp[j];
+        d = fmaf(q[4 * j], k4.x, d);
+        d = fmaf(q[4 * j + 1], k4.y, d);
+        d = fmaf(q[4 * j + 2], k4.z, d);
+        d = fmaf(q[4 * j + 3], k4.w, d);
+      }
+    }
+#pragma unroll
+    for (int off = G / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+    d = __fdiv_rn(d, denom);
+    if (t < T) {
+      if (part == 0) s[t] = d;
+      mx = fmaxf(mx, d);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  __syncwarp();
+  float sum = 0.0f;
+  for (int t = lane; t < T; t += 32) {
+    const float e = expf(s[t] - mx);
+    s[t] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  __syncwarp();
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+  for (int t0 = 0; t0 < T; t0 += P) {
+    const int t = t0 + slot;
+    if (t < T) {
+      const float wt = __fdiv_rn(s[t], sum);
+      const float4* vp = reinterpret_cast<const float4*>(vb + (int64_t)t * kvr);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 v4 = vp[j];
+        acc[4 * j] = fmaf(wt, v4.x, acc[4 * j]);
+        acc[4 * j + 1] = fmaf(wt, v4.y, acc[4 * j + 1]);
+        acc[4 * j + 2] = fmaf(wt, v4.z, acc[4 * j + 2]);
+        acc[4 * j + 3] = fmaf(wt, v4.w, acc[4 * j + 3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = G; off < 32; off <<= 1)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
+  if (slot == 0) {
+    float4* op = reinterpret_cast<float4*>(o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      op[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+  }
+}
+
+struct StopSet {
+  int32_t n, min_new;
+  int32_t ids[kMaxStop];
+};
+
+// Greedy control for one step (torch_benchmark.py:272-293 at temperature 0,
+// prepare_e2e.py:129-143): consume the argmax key, record the pick, stop on
+// a stop id once min_new_tokens exist, otherwise feed the next token.
+__global__ void advance_kernel(int n, Work w, const int32_t* __restrict__ prompts, int32_t stride,
+                               int32_t new_tokens, StopSet stop, int32_t* sampled,
+                               int32_t* n_sampled, int32_t* stop_reason) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n; b += gridDim.x * blockDim.x) {
+    const unsigned long long key = w.keys[b];
+    w.keys[b] = 0ull;
+    const int f = w.flags[b];
+    if (f & (SEQ_DONE | SEQ_INVALID)) {
+      w.flags[b] = f | SEQ_DONE;
+      continue;
+    }
+    const int p = w.pos[b], L = w.plen[b];
+    if (p < L - 1) {  // still inside the prompt
+      w.tok[b] = prompts[(int64_t)b * stride + p + 1];
+      w.pos[b] = p + 1;
+      continue;
+    }
+    const int g = w.gen[b];
+    const int t = argmax_index(key);
+    sampled[(int64_t)b * new_tokens + g] = t;
+    n_sampled[b] = g + 1;
+    bool is_stop = false;
+    for (int i = 0; i < stop.n; ++i) is_stop |= (stop.ids[i] == t);
+    if (is_stop && g >= stop.min_new) {
+      stop_reason[b] = t;
+      w.flags[b] = f | SEQ_DONE;
+      continue;
+    }
+    w.gen[b] = g + 1;
+    if (g + 1 >= new_tokens) {
+      w.flags[b] = f | SEQ_DONE;
+      continue;
+    }
+    w.tok[b] = t;
+    w.pos[b] = p + 1;
+  }
+}
+
+__global__ void keys_to_argmax_kernel(int n, unsigned long long* keys, int32_t* argmax) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n; b += gridDim.x * blockDim.x) {
+    argmax[b] = argmax_index(keys[b]);
+    keys[b] = 0ull;
+  }
+}
+
+// ---- step enqueue --------------------------------------------------------------
+
+static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc, float* vc,
+                            int64_t cstride, const EpiArgs& vocab_ep, cudaStream_t st) {
+  const q6w_model_desc& d = M->d;
+  const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
+  embed_kernel<<<n < 2048 ? n : 2048, 128, 0, st>>>(d.tok_embeddings.packed,
+                                                    d.tok_embeddings.scales, dim, d.vocab_size, S,
+                                                    n, w);
+  Q6W_LAUNCH_CHECK("embed_kernel");
+  EpiArgs ep;
+  memset(&ep, 0, sizeof(ep));
+  ep.pos = w.pos;
+  ep.flags = w.flags;
+  const int warps = d.n_heads < 8 ? d.n_heads : 8;
+  const dim3 agrid(n, (d.n_heads + warps - 1) / warps);
+  const size_t asmem = (size_t)warps * S * sizeof(float);
+  for (int l = 0; l < d.n_layers; ++l) {
+    const q6w_layer_weights& L = M->layers[l];
+    const int64_t layer_off = (int64_t)l * S * kvr;
+    cudaError_t e;
+    {
+      MatSet ms = {L.wq.packed, L.wk.packed, L.wv.packed, L.wq.scales, L.wk.scales, L.wv.scales,
+                   dim, dim + kvr, dim, 0, (dim + 2 * kvr) / 2};
+      EpiArgs q = ep;
+      q.qbuf = w.qb;
+      q.ldq = dim;
+      q.kc = kc;
+      q.vc = vc;
+      q.cache_stride = cstride;
+      q.layer_off = layer_off;
+      q.rope_cos = d.rope_cos;
+      q.rope_sin = d.rope_sin;
+      q.hd = M->hd;
+      q.q_rows = dim;
+      q.kv_rows = kvr;
+      e = LinearLauncher<true, EPI_QKV>::run(w.x, dim, n, L.attention_norm, d.norm_eps, ms, q, st);
+      if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "qkv linear: %s", cudaGetErrorString(e));
+    }
+    switch (M->hd) {
+#define Q6W_ATTN(HDV)                                                                          \
+  case HDV:                                                                                    \
+    attn_kernel<HDV / 16><<<agrid, warps * 32, asmem, st>>>(w.qb, dim, kc, vc, cstride,        \
+                                                            layer_off, w.pos, 1, w.flags, w.att, \
+                                                            dim, d.n_heads, d.n_kv_heads, S,   \
+                                                            M->denom);                         \
+    break;
+      Q6W_ATTN(16) Q6W_ATTN(32) Q6W_ATTN(64) Q6W_ATTN(128) Q6W_ATTN(256) Q6W_ATTN(512)
+#undef Q6W_ATTN
+      default:
+        return fail(Q6W_ERR_ARG, "unsupported head_dim %d", M->hd);
+    }
+    Q6W_LAUNCH_CHECK("attn_kernel");
+    {
+      MatSet ms = {L.wo.packed, nullptr, nullptr, L.wo.scales, nullptr, nullptr,
+                   dim, dim, dim, 0, dim / 2};
+      EpiArgs r = ep;
+      r.y = w.x;
+      r.ldy = dim;
+      e = LinearLauncher<false, EPI_RESID>::run(w.att, dim, n, nullptr, 0.f, ms, r, st);
+      if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "wo linear: %s", cudaGetErrorString(e));
+    }
+    {
+      MatSet ms = {L.w1.packed, L.w3.packed, nullptr, L.w1.scales, L.w3.scales, nullptr,
+                   hid, hid, dim, 1, hid};
+      EpiArgs gl = ep;
+      gl.y = w.hb;
+      gl.ldy = hid;
+      e = LinearLauncher<true, EPI_GLU>::run(w.x, dim, n, L.ffn_norm, d.norm_eps, ms, gl, st);
+      if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "w1/w3 linear: %s", cudaGetErrorString(e));
+    }
+    {
+      MatSet ms = {L.w2.packed, nullptr, nullptr, L.w2.scales, nullptr, nullptr,
+                   dim, dim, hid, 0, dim / 2};
+      EpiArgs r = ep;
+      r.y = w.x;
+      r.ldy = dim;
+      e = LinearLauncher<false, EPI_RESID>::run(w.hb, hid, n, nullptr, 0.f, ms, r, st);
+      if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "w2 linear: %s", cudaGetErrorString(e));
+    }
+  }
+  MatSet mv = {d.tok_embeddings.packed, nullptr, nullptr, d.tok_embeddings.scales, nullptr, nullptr,
+               d.vocab_size, d.vocab_size, dim, 0, d.vocab_size / 2};
+  EpiArgs v = vocab_ep;
+  v.pos = w.pos;
+  v.flags = w.flags;
+  v.keys = w.keys;
+  v.gen = w.gen;
+  v.plen = w.plen;
+  v.vocab = d.vocab_size;
+  cudaError_t e = LinearLauncher<true, EPI_VOCAB>::run(w.x, dim, n, d.norm, d.norm_eps, mv, v, st);
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "vocab linear: %s", cudaGetErrorString(e));
+  return Q6W_OK;
+}
+
+static int32_t check_qmat(const q6w_qmat& m, int rows, int cols, const char* name) {
+  if (!m.packed || !m.scales) return fail(Q6W_ERR_ARG, "%s: null pointer", name);
+  if (m.rows != rows || m.cols != cols)
+    return fail(Q6W_ERR_ARG, "%s: shape [%d, %d], expected [%d, %d]", name, m.rows, m.cols, rows, cols);
+  if (!aligned(m.packed, 4) || !aligned(m.scales, 4))
+    return fail(Q6W_ERR_ALIGN, "%s: packed rows and scales must be 4-byte aligned", name);
+  return Q6W_OK;
+}
+
+static int attn_smem_ok(const q6w_model* M) {
+  const int warps = M->d.n_heads < 8 ? M->d.n_heads : 8;
+  return (size_t)warps * M->d.max_seq_len * sizeof(float) <= 200 * 1024;
+}
+
+static int32_t set_attn_attrs(const q6w_model* M) {
+  const int warps = M->d.n_heads < 8 ? M->d.n_heads : 8;
+  const int smem = warps * M->d.max_seq_len * (int)sizeof(float);
+  if (smem <= 48 * 1024) return Q6W_OK;
+  cudaError_t e = cudaSuccess;
+  switch (M->hd) {
+    case 16: e = cudaFuncSetAttribute(attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 32: e = cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 64: e = cudaFuncSetAttribute(attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 128: e = cudaFuncSetAttribute(attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 256: e = cudaFuncSetAttribute(attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 512: e = cudaFuncSetAttribute(attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+  }
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
+  return Q6W_OK;
+}
+
+}  // namespace q6w
+
+using namespace q6w;
+
+extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out) {
+  clear_error();
+  if (!desc || !out) return fail(Q6W_ERR_ARG, "q6w_model_create: null argument");
+  *out = nullptr;
+  const q6w_model_desc& d = *desc;
+  if (d.dim <= 0 || d.n_layers <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.vocab_size <= 0 ||
+      d.hidden_dim <= 0 || d.max_seq_len <= 0)
+    return fail(Q6W_ERR_ARG, "model dimensions must be positive");
+  if (d.dim % d.n_heads || d.n_heads % d.n_kv_heads)
+    return fail(Q6W_ERR_ARG, "dim %% n_heads and n_heads %% n_kv_heads must be 0");
+  const int hd = d.dim / d.n_heads;
+  if (hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256 && hd != 512)
+    return fail(Q6W_ERR_ARG, "head_dim %d unsupported (16, 32, 64, 128, 256 or 512)", hd);
+  if (d.dim % 16 || d.hidden_dim % 16)
+    return fail(Q6W_ERR_ARG, "dim and hidden_dim must be multiples of 16");
+  if (d.vocab_size % 2) return fail(Q6W_ERR_ARG, "vocab_size must be even");
+  if (!(d.norm_eps >= 0.0f)) return fail(Q6W_ERR_ARG, "norm_eps must be >= 0");
+  if (!d.layers || !d.norm || !d.rope_cos || !d.rope_sin)
+    return fail(Q6W_ERR_ARG, "q6w_model_create: null weight pointer");
+  const int kvr = d.n_kv_heads * hd;
+  int32_t st = check_qmat(d.tok_embeddings, d.vocab_size, d.dim, "tok_embeddings");
+  if (st) return st;
+  for (int l = 0; l < d.n_layers; ++l) {
+    const q6w_layer_weights& L = d.layers[l];
+    if ((st = check_qmat(L.wq, d.dim, d.dim, "wq")) || (st = check_qmat(L.wk, kvr, d.dim, "wk")) ||
+        (st = check_qmat(L.wv, kvr, d.dim, "wv")) || (st = check_qmat(L.wo, d.dim, d.dim, "wo")) ||
+        (st = check_qmat(L.w1, d.hidden_dim, d.dim, "w1")) ||
+        (st = check_qmat(L.w2, d.dim, d.hidden_dim, "w2")) ||
+        (st = check_qmat(L.w3, d.hidden_dim, d.dim, "w3")))
+      return st;
+    if (!L.attention_norm || !L.ffn_norm) return fail(Q6W_ERR_ARG, "layer %d: null norm", l);
+  }
+  q6w_model* M = new (std::nothrow) q6w_model();
+  if (!M) return fail(Q6W_ERR_ARG, "out of host memory");
+  M->d = d;
+  M->layers.assign(d.layers, d.layers + d.n_layers);
+  M->d.layers = M->layers.data();
+  M->hd = hd;
+  M->kv_rows = kvr;
+  M->denom = (float)sqrt((double)hd);
+  cudaGetDevice(&M->device);
+  if (!attn_smem_ok(M)) {
+    delete M;
+    return fail(Q6W_ERR_ARG, "max_seq_len %d too large for the attention score buffer", d.max_seq_len);
+  }
+  if ((st = set_attn_attrs(M))) {
+    delete M;
+    return st;
+  }
+  *out = M;
+  return Q6W_OK;
+}
+
+extern "C" void q6w_model_destroy(q6w_model* M) {
+  if (!M) return;
+  if (M->exec) cudaGraphExecDestroy(M->exec);
+  if (M->cap_stream) cudaStreamDestroy(M->cap_stream);
+  delete M;
+}
+
+extern "C" size_t q6w_workspace_bytes(const q6w_model* M, int32_t max_seqs) {
+  if (!M || max_seqs < 0) return 0;
+  return layout(M, max_seqs, nullptr, nullptr);
+}
+
+static int32_t check_ws(const q6w_model* M, int n, void* ws, size_t bytes, Work* w) {
+  if (!ws) return fail(Q6W_ERR_ARG, "null workspace");
+  if (!aligned(ws, 256)) return fail(Q6W_ERR_ALIGN, "workspace must be 256-byte aligned");
+  if (layout(M, n, nullptr, nullptr) > bytes)
+    return fail(Q6W_ERR_ARG, "workspace of %zu bytes too small for %d sequences (%zu needed)", bytes, n,
+                layout(M, n, nullptr, nullptr));
+  layout(M, n, (char*)ws, w);
+  return Q6W_OK;
+}
+
+static int32_t check_cache(const q6w_model* M, const float* kc, const float* vc, int64_t stride, int n) {
+  if (!kc || !vc) return fail(Q6W_ERR_ARG, "null KV cache");
+  if (!aligned(kc, 16) || !aligned(vc, 16)) return fail(Q6W_ERR_ALIGN, "KV cache must be 16-byte aligned");
+  const int64_t per = (int64_t)M->d.n_layers * M->d.max_seq_len * M->kv_rows;
+  if (n > 1 && (stride < per || stride % 4))
+    return fail(Q6W_ERR_ARG, "cache_seq_stride %lld must be >= %lld and a multiple of 4", (long long)stride,
+                (long long)per);
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_step(const q6w_model* M, int32_t token_id, int32_t position, float* k_cache,
+                            float* v_cache, float* logits, void* workspace, size_t workspace_bytes,
+                            q6w_stream_t stream) {
+  clear_error();
+  if (!M) return fail(Q6W_ERR_ARG, "null model");
+  if (token_id < 0 || token_id >= M->d.vocab_size)
+    return fail(Q6W_ERR_RANGE, "token id %d outside [0, %d)", token_id, M->d.vocab_size);
+  if (position < 0 || position >= M->d.max_seq_len)
+    return fail(Q6W_ERR_RANGE, "position %d outside [0, %d)", position, M->d.max_seq_len);
+  if (!logits || !aligned(logits, 8)) return fail(Q6W_ERR_ARG, "logits must be non-null and 8-byte aligned");
+  Work w;
+  int32_t st = check_ws(M, 1, workspace, workspace_bytes, &w);
+  if (st) return st;
+  if ((st = check_cache(M, k_cache, v_cache, 0, 1))) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  init_batch_kernel<<<1, 32, 0, s>>>(1, nullptr, nullptr, token_id, position, w);
+  Q6W_LAUNCH_CHECK("init_batch_kernel");
+  EpiArgs v;
+  memset(&v, 0, sizeof(v));
+  v.y = logits;
+  v.ldy = M->d.vocab_size;
+  return enqueue_step(M, 1, w, k_cache, v_cache, 0, v, s);
+}
+
+extern "C" int32_t q6w_forward_batch(const q6w_model* M, int32_t n, const int32_t* tokens,
+                                     const int32_t* positions, float* k_cache, float* v_cache,
+                                     int64_t cache_seq_stride, float* logits, int32_t* argmax,
+                                     void* workspace, size_t workspace_bytes, q6w_stream_t stream) {
+  clear_error();
+  if (!M) return fail(Q6W_ERR_ARG, "null model");
+  if (n < 0) return fail(Q6W_ERR_ARG, "n_seqs must be >= 0");
+  if (n == 0) return Q6W_OK;
+  if (!tokens || !positions) return fail(Q6W_ERR_ARG, "null tokens/positions");
+  if (logits && !aligned(logits, 8)) return fail(Q6W_ERR_ALIGN, "logits must be 8-byte aligned");
+  Work w;
+  int32_t st = check_ws(M, n, workspace, workspace_bytes, &w);
+  if (st) return st;
+  if ((st = check_cache(M, k_cache, v_cache, cache_seq_stride, n))) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  init_batch_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, tokens, positions, 0, 0, w);
+  Q6W_LAUNCH_CHECK("init_batch_kernel");
+  EpiArgs v;
+  memset(&v, 0, sizeof(v));
+  v.y = logits;
+  v.ldy = M->d.vocab_size;
+  if ((st = enqueue_step(M, n, w, k_cache, v_cache, cache_seq_stride, v, s))) return st;
+  if (argmax) {
+    keys_to_argmax_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, w.keys, argmax);
+    Q6W_LAUNCH_CHECK("keys_to_argmax_kernel");
+  }
+  return Q6W_OK;
+}
+
+static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& w,
+                            const StopSet& stop) {
+  if (!M->cap_stream) Q6W_CUDA_TRY(cudaStreamCreateWithFlags(&M->cap_stream, cudaStreamNonBlocking));
+  if (M->exec) {
+    cudaGraphExecDestroy(M->exec);
+    M->exec = nullptr;
+    M->have_key = false;
+  }
+  Q6W_CUDA_TRY(cudaStreamBeginCapture(M->cap_stream, cudaStreamCaptureModeRelaxed));
+  EpiArgs v;
+  memset(&v, 0, sizeof(v));
+  v.step_logits = a->step_logits;
+  v.new_tokens = a->new_tokens;
+  v.min_new = stop.min_new;
+  v.n_stop = stop.n;
+  for (int i = 0; i < kMaxStop; ++i) v.stop_ids[i] = stop.ids[i];
+  int32_t st = enqueue_step(M, a->n_seqs, w, a->k_cache, a->v_cache, a->cache_seq_stride, v,
+                            M->cap_stream);
+  if (st == Q6W_OK) {
+    advance_kernel<<<grid_for(a->n_seqs, 256), 256, 0, M->cap_stream>>>(
+        a->n_seqs, w, a->prompts, a->prompt_stride, a->new_tokens, stop, a->sampled, a->n_sampled,
+        a->stop_reason);
+    if (cudaGetLastError() != cudaSuccess) st = fail(Q6W_ERR_CUDA, "advance_kernel launch failed");
+  }
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(M->cap_stream, &graph);
+  if (st) {
+    if (graph) cudaGraphDestroy(graph);
+    return st;
+  }
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&M->exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    M->exec = nullptr;
+    return fail(Q6W_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+  }
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, void* workspace,
+                                       size_t workspace_bytes, q6w_stream_t stream) {
+  clear_error();
+  if (!M || !a) return fail(Q6W_ERR_ARG, "null argument");
+  const int n = a->n_seqs;
+  if (n < 0) return fail(Q6W_ERR_ARG, "n_seqs must be >= 0");
+  if (n == 0) return Q6W_OK;
+  if (!a->prompts || !a->prompt_lens || !a->sampled || !a->n_sampled || !a->stop_reason)
+    return fail(Q6W_ERR_ARG, "null prompt/output pointer");
+  if (a->max_prompt_len < 1 || a->prompt_stride < a->max_prompt_len)
+    return fail(Q6W_ERR_ARG, "need 1 <= max_prompt_len <= prompt_stride");
+  if (a->new_tokens < 1) return fail(Q6W_ERR_ARG, "new_tokens must be >= 1");
+  if ((int64_t)a->max_prompt_len + a->new_tokens - 1 > M->d.max_seq_len)
+    return fail(Q6W_ERR_RANGE, "prompt plus generated tokens exceeds the model context (%d)", M->d.max_seq_len);
+  if (a->n_stop < 0 || a->n_stop > kMaxStop || (a->n_stop && !a->stop_ids))
+    return fail(Q6W_ERR_ARG, "n_stop must be in [0, %d]", kMaxStop);
+  if (a->min_new_tokens < 0 || a->min_new_tokens > a->new_tokens)
+    return fail(Q6W_ERR_ARG, "min_new_tokens must be within the token limit");
+  if (a->step_logits && !aligned(a->step_logits, 8)) return fail(Q6W_ERR_ALIGN, "step_logits must be 8-byte aligned");
+  StopSet stop;
+  memset(&stop, 0, sizeof(stop));
+  stop.n = a->n_stop;
+  stop.min_new = a->min_new_tokens;
+  for (int i = 0; i < a->n_stop; ++i) {
+    if (a->stop_ids[i] < 0 || a->stop_ids[i] >= M->d.vocab_size)
+      return fail(Q6W_ERR_RANGE, "stop id %d outside the vocabulary", a->stop_ids[i]);
+    stop.ids[i] = a->stop_ids[i];
+  }
+  Work w;
+  int32_t st = check_ws(M, n, workspace, workspace_bytes, &w);
+  if (st) return st;
+  if ((st = check_cache(M, a->k_cache, a->v_cache, a->cache_seq_stride, n))) return st;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != M->device) return fail(Q6W_ERR_ARG, "model was created on device %d, current is %d", M->device, dev);
+
+  GraphKey key;
+  memset(&key, 0, sizeof(key));
+  key.a = *a;
+  key.a.stop_ids = nullptr;
+  key.a.prefill_event = nullptr;
+  memcpy(key.stop, stop.ids, sizeof(key.stop));
+  key.ws = workspace;
+  if (!M->exec || !M->have_key || memcmp(&key, &M->key, sizeof(key)) != 0) {
+    if ((st = capture_step(M, a, w, stop))) return st;
+    M->key = key;
+    M->have_key = true;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  init_greedy_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, a->prompts, a->prompt_lens, a->prompt_stride,
+                                                      a->max_prompt_len, w, a->n_sampled, a->stop_reason);
+  Q6W_LAUNCH_CHECK("init_greedy_kernel");
+  const int steps = a->max_prompt_len + a->new_tokens - 1;
+  for (int i = 0; i < steps; ++i) {
+    Q6W_CUDA_TRY(cudaGraphLaunch(M->exec, s));
+    if (i + 1 == a->max_prompt_len && a->prefill_event)
+      Q6W_CUDA_TRY(cudaEventRecord((cudaEvent_t)a->prefill_event, s));
+  }
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_workspace_status(void* workspace, q6w_stream_t stream) {
+  clear_error();
+  if (!workspace) return fail(Q6W_ERR_ARG, "null workspace");
+  cudaStream_t s = (cudaStream_t)stream;
+  int32_t flag = 0;
+  Q6W_CUDA_TRY(cudaMemcpyAsync(&flag, workspace, sizeof(flag), cudaMemcpyDeviceToHost, s));
+  Q6W_CUDA_TRY(cudaStreamSynchronize(s));
+  if (flag) {
+    Q6W_CUDA_TRY(cudaMemsetAsync(workspace, 0, sizeof(flag), s));
+    Q6W_CUDA_TRY(cudaStreamSynchronize(s));
+    return fail(Q6W_ERR_DEVICE, "a kernel rejected a token, position or prompt length (sequence skipped)");
+  }
+  return Q6W_OK;
+}
+
+static int32_t attn_attr(int hd, int smem) {
+  if (smem <= 48 * 1024) return Q6W_OK;
+  cudaError_t e = cudaSuccess;
+  switch (hd) {
+    case 16: e = cudaFuncSetAttribute(attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 32: e = cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 64: e = cudaFuncSetAttribute(attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 128: e = cudaFuncSetAttribute(attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 256: e = cudaFuncSetAttribute(attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+    case 512: e = cudaFuncSetAttribute(attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); break;
+  }
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_gqa_attention(const float* queries, const float* keys, const float* values,
+                                     float* output, const int32_t* lengths, int32_t n,
+                                     int32_t kv_heads, int32_t groups_per_kv, int32_t head_dim,
+                                     int32_t max_len, int64_t kv_seq_stride, q6w_stream_t stream) {
+  clear_error();
+  if (n < 0 || kv_heads <= 0 || groups_per_kv <= 0 || max_len <= 0)
+    return fail(Q6W_ERR_ARG, "q6w_gqa_attention: n >= 0, kv_heads, groups_per_kv, max_len > 0 required");
+  if (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512)
+    return fail(Q6W_ERR_ARG, "head_dim %d unsupported (16, 32, 64, 128, 256 or 512)", head_dim);
+  if (n == 0) return Q6W_OK;
+  if (!queries || !keys || !values || !output || !lengths) return fail(Q6W_ERR_ARG, "q6w_gqa_attention: null pointer");
+  if (!aligned(queries, 16) || !aligned(keys, 16) || !aligned(values, 16) || !aligned(output, 16))
+    return fail(Q6W_ERR_ALIGN, "q6w_gqa_attention: tensors must be 16-byte aligned");
+  const int64_t per = (int64_t)max_len * kv_heads * head_dim;
+  if (n > 1 && (kv_seq_stride < per || kv_seq_stride % 4))
+    return fail(Q6W_ERR_ARG, "kv_seq_stride must be >= max_len*kv_heads*head_dim and a multiple of 4");
+  const int H = kv_heads * groups_per_kv;
+  const int warps = H < 8 ? H : 8;
+  const size_t smem = (size_t)warps * max_len * sizeof(float);
+  if (smem > 200 * 1024) return fail(Q6W_ERR_ARG, "max_len %d too large", max_len);
+  int32_t st = attn_attr(head_dim, (int)smem);
+  if (st) return st;
+  const dim3 grid(n, (H + warps - 1) / warps);
+  const float denom = (float)sqrt((double)head_dim);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int ld = H * head_dim;
+  switch (head_dim) {
+#define Q6W_ATTN2(HDV)                                                                               \
+  case HDV:                                                                                          \
+    attn_kernel<HDV / 16><<<grid, warps * 32, smem, s>>>(queries, ld, keys, values, kv_seq_stride, 0, \
+                                                         lengths, 0, nullptr, output, ld, H,         \
+                                                         kv_heads, max_len, denom);                  \
+    break;
+    Q6W_ATTN2(16) Q6W_ATTN2(32) Q6W_ATTN2(64) Q6W_ATTN2(128) Q6W_ATTN2(256) Q6W_ATTN2(512)
+#undef Q6W_ATTN2
+  }
+  Q6W_LAUNCH_CHECK("attn_kernel");
+  return Q6W_OK;
+}
