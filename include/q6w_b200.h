@@ -85,6 +85,23 @@ Q6W_API int32_t q6w_linear_argmax(const uint8_t* packed, const float* scales, co
                                   size_t scratch_bytes, int64_t rows, int64_t cols, int64_t n,
                                   q6w_stream_t stream);
 
+/* q6w_linear_argmax without caller scratch: no counterpart in the reference.
+ * For callers that cannot allocate device memory -- hosts binding this
+ * library through a plain FFI (ctypes, JNI, cgo) that own no CUDA allocator,
+ * and serving loops under a fixed device-memory budget where a per-call
+ * cudaMalloc can fail and cudaFree synchronises the device.  The argmax keys
+ * live in a library-owned device array of 32768 entries (256 KiB, held by
+ * every GPU that loads the library until exit), so n <= 32768; larger n is
+ * rejected with Q6W_ERR_ARG.  Allocates nothing.  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the one array
+ * (cleared at the start of each call): calls that overlap on the GPU, on
+ * any streams, race and must be serialised by the caller. */
+Q6W_API int32_t q6w_linear_argmax_noalloc(const uint8_t* packed, const float* scales,
+                                          const float* x, float* logits, int32_t* argmax,
+                                          int64_t rows, int64_t cols, int64_t n,
+                                          q6w_stream_t stream);
+
 /* out[s, :] = x[s, :] * (1 / sqrt(mean(x[s, :]^2) + eps)) * weight, for n
  * rows of `length` (torch_benchmark.py:22-24).  Replaces
  * arm_neon_rmsnorm_f32 (scripts/neon_rmsnorm.c:4-31). */

@@ -1,6 +1,8 @@
 // q6w_linear: y[n, rows] = x[n, cols] @ dequant(W)^T, the Q6W nn.Linear.
 #include <string.h>
 
+#include <mutex>
+
 #include "linear.cuh"
 
 namespace q6w {
@@ -134,5 +136,86 @@ extern "C" int32_t q6w_linear(const uint8_t* packed, const float* scales, const 
   ep.ldy = (int32_t)rows;
   cudaError_t e = LinearLauncher<false, EPI_STORE>::run(x, (int)cols, (int)n, nullptr, 0.f, ms, ep, st);
   if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "q6w_linear launch: %s", cudaGetErrorString(e));
+  return Q6W_OK;
+}
+
+// ---- q6w_linear_argmax_noalloc ----------------------------------------------
+//
+// Same computation as q6w_linear_argmax, with its scratch (one 64-bit argmax
+// key per activation row) in a library-owned device array instead of caller
+// memory, for callers that cannot allocate device memory: hosts that bind
+// this library through a plain FFI (ctypes, JNI, cgo) and own no CUDA
+// allocator, and serving loops that run under a fixed device-memory budget
+// where a per-call cudaMalloc can fail and a cudaFree synchronises the
+// device.  Every GPU that loads the library holds the array (256 KiB) until
+// the process exits.
+namespace q6w {
+
+constexpr int64_t kNoAllocMaxRows = 32768;  // activation rows per call
+static __device__ __align__(256) unsigned long long g_noalloc_keys[kNoAllocMaxRows];
+
+// Device address of g_noalloc_keys, looked up once per device (the host-side
+// name is only a stand-in for the symbol, not a device pointer).
+static unsigned long long* noalloc_keys_ptr(int32_t* status) {
+  static std::mutex mu;
+  static unsigned long long* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = fail(Q6W_ERR_CUDA, "q6w_linear_argmax_noalloc: cannot query the current device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_keys);
+    if (e != cudaSuccess || !p) {
+      *status = fail(Q6W_ERR_CUDA, "q6w_linear_argmax_noalloc: cudaGetSymbolAddress failed: %s",
+                     cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = (unsigned long long*)p;
+  }
+  *status = Q6W_OK;
+  return ptrs[dev];
+}
+
+}  // namespace q6w
+
+extern "C" int32_t q6w_linear_argmax_noalloc(const uint8_t* packed, const float* scales,
+                                             const float* x, float* logits, int32_t* argmax,
+                                             int64_t rows, int64_t cols, int64_t n,
+                                             q6w_stream_t stream) {
+  clear_error();
+  if (n > kNoAllocMaxRows)
+    return fail(Q6W_ERR_ARG,
+                "q6w_linear_argmax_noalloc: n = %lld activation rows exceeds the built-in maximum of %lld",
+                (long long)n, (long long)kNoAllocMaxRows);
+  if (rows <= 0 || cols <= 0 || n < 0) return fail(Q6W_ERR_ARG, "q6w_linear_argmax_noalloc: bad shape");
+  if (cols % 16 || rows % 2)
+    return fail(Q6W_ERR_ARG, "q6w_linear_argmax_noalloc: cols %% 16 == 0 and even rows required");
+  if (rows > INT32_MAX / 2 || cols > INT32_MAX / 2) return fail(Q6W_ERR_ARG, "q6w_linear_argmax_noalloc: shape too large");
+  if (n == 0) return Q6W_OK;
+  if (!packed || !scales || !x || !argmax) return fail(Q6W_ERR_ARG, "q6w_linear_argmax_noalloc: null pointer");
+  if (!aligned(packed, 4) || !aligned(scales, 4) || !aligned(x, 16) || (logits && !aligned(logits, 8)) ||
+      !aligned(argmax, 4))
+    return fail(Q6W_ERR_ALIGN, "q6w_linear_argmax_noalloc: misaligned pointer");
+  int32_t st = Q6W_OK;
+  unsigned long long* keys = noalloc_keys_ptr(&st);
+  if (!keys) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  // The array keeps the previous call's contents: the keys must start at 0.
+  Q6W_CUDA_TRY(cudaMemsetAsync(keys, 0, (size_t)n * sizeof(unsigned long long), s));
+  MatSet ms = {packed, nullptr, nullptr, scales, nullptr, nullptr,
+               (int32_t)rows, (int32_t)rows, (int32_t)cols, 0, (int32_t)(rows / 2)};
+  EpiArgs ep;
+  memset(&ep, 0, sizeof(ep));
+  ep.y = logits;
+  ep.ldy = (int32_t)rows;
+  ep.keys = keys;
+  cudaError_t e = LinearLauncher<false, EPI_VOCAB>::run(x, (int)cols, (int)n, nullptr, 0.f, ms, ep, s);
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "q6w_linear_argmax_noalloc launch: %s", cudaGetErrorString(e));
+  keys_to_index_kernel<<<grid_for(n, 256), 256, 0, s>>>((int)n, keys, argmax);
+  Q6W_LAUNCH_CHECK("keys_to_index_kernel");
   return Q6W_OK;
 }
