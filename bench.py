@@ -293,6 +293,8 @@ def run_b200(a):
 
     # ---- dominant kernel alone: decode attention over this run's caches
     roof = attention_roofline(model, caches, n, P + T - 1, stream)
+    b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if rank == 0 else None
+    gemv = scaled_gemv(dev, stream) if rank == 0 else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -312,6 +314,7 @@ def run_b200(a):
                     "d2h_bytes_per_step": int(n * T * 4)},
             "gpu_launches": launches_per_gen * a.steps,
             "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len,
+            "b1": b1, "gemv_scaled": gemv,
         }
         if not a.no_cpu_baseline and world == 1:
             cores = cpu_cores()
@@ -326,6 +329,93 @@ def run_b200(a):
         dist.barrier()
         dist.destroy_process_group()
     tmp.cleanup()
+
+
+def b1_latency(model, prompt, new_tokens, stream, reps=5):
+    """B=1 greedy request of the tiny model (20-token prompt + 128 tokens), the
+    reference's own headline request shape: device loop, CUDA events."""
+    import torch
+
+    dev = model.device
+    pr = torch.tensor([prompt], dtype=torch.int32, device=dev)
+    ln = torch.tensor([len(prompt)], dtype=torch.int32, device=dev)
+    caches = model.new_batch_cache(1)
+    for _ in range(3):
+        model.generate_greedy_device(pr, ln, len(prompt), new_tokens, caches=caches)
+    torch.cuda.synchronize()
+    tot, dec = [], []
+    for _ in range(reps):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        e1.record(stream)
+        model.generate_greedy_device(pr, ln, len(prompt), new_tokens, caches=caches, prefill_event=e1)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        tot.append(e0.elapsed_time(e2) / 1e3)
+        dec.append(e1.elapsed_time(e2) / 1e3)
+    t, d = statistics.median(tot), statistics.median(dec)
+    steps = len(prompt) + new_tokens - 1
+    return {"workload": f"B=1 greedy, {len(prompt)}-token prompt + {new_tokens} tokens, tiny model",
+            "request_tok_s": round(new_tokens / t, 1), "decode_tok_s": round(new_tokens / d, 1),
+            "us_per_model_step": round(t / steps * 1e6, 2), "prefill_ms": round((t - d) * 1e3, 3)}
+
+
+def scaled_gemv(dev, stream, reps=10):
+    """HBM-streaming Q6W GEMV at B=1 on the 1.1B-shape config's matrices
+    (22 layers of wq/wk/wv/wo/w1/w2/w3 at dim 2048, hidden 5632, kv 256, plus
+    the 32000x2048 vocab): one pass over 777 MB of packed weights per token,
+    replayed from a CUDA graph.  Weights are random bytes (every byte pattern
+    is a valid Q6W code stream); the cost does not depend on the values."""
+    import torch
+
+    from q6w_b200 import _lib
+
+    lib = _lib.load()
+    dim, hid, kv, vocab, layers = 2048, 5632, 256, 32000, 22
+    shapes = [(dim, dim), (kv, dim), (kv, dim), (dim, dim), (hid, dim), (dim, hid), (hid, dim)] * layers
+    shapes.append((vocab, dim))
+    nbytes = sum(r * c * 3 // 4 + 4 * r for r, c in shapes)
+    blob = torch.randint(0, 256, (nbytes + 256 * len(shapes),), dtype=torch.uint8, device=dev)
+    mats, off = [], 0
+    for r, c in shapes:
+        pb = r * c * 3 // 4
+        q = blob[off: off + pb]
+        off = (off + pb + 255) // 256 * 256
+        sc = blob[off: off + 4 * r].view(torch.float32)
+        off = (off + 4 * r + 255) // 256 * 256
+        mats.append((q, sc, r, c))
+    for _, sc, r, _ in mats:  # finite, positive row scales
+        sc.copy_(torch.rand(r, device=dev) * 0.05 + 0.001)
+    x = torch.randn(max(dim, hid), device=dev)
+    ys = [torch.empty(r, device=dev) for r, _ in shapes]
+    def run(st):
+        h = _lib.stream_handle(st)
+        for (q, sc, r, c), y in zip(mats, ys):
+            _lib.check(lib.q6w_linear(q.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(), r, c, 1, h))
+
+    run(stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    with torch.cuda.graph(g, stream=side):
+        run(side)
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    moved = nbytes + sum(4 * (r + c) for r, c in shapes)
+    peak, kind = measured_peaks()
+    del g
+    return {"workload": "B=1 Q6W GEMV pass over the 1.1B-shape matrices (155 launches, CUDA graph)",
+            "bytes_per_token": moved, "us_per_token": round(sec * 1e6, 2),
+            "achieved_gbs": round(moved / sec / 1e9, 1), "peak_gbs": peak,
+            "frac": round(moved / sec / 1e9 / peak, 4), "peak_kind": f"{kind} hbm_gbs",
+            "weights_tok_s_ceiling": round(1 / sec, 1)}
 
 
 def attention_roofline(model, caches, n, length, stream):

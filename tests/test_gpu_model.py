@@ -231,3 +231,33 @@ def test_gqa_attention_op(tiny):
         w = torch.softmax((q[i].unsqueeze(1) @ ks.transpose(1, 2)) / hd ** 0.5, -1)
         want = (w @ vs).squeeze(1)
         assert (out[i] - want).abs().max() <= 1e-5
+
+
+@pytest.mark.parametrize("n", [64, 130, 513])
+def test_tensor_core_step_matches_simt_step(tiny_files, monkeypatch, n):
+    """The tcgen05 batched step (n >= 64) against the FP32 SIMT step on the
+    same inputs, and both against the oracle on a sample of sequences."""
+    tc_model = Q6WCudaTransformer.from_q6w(*tiny_files)
+    monkeypatch.setenv("Q6W_DISABLE_TC", "1")
+    simt_model = Q6WCudaTransformer.from_q6w(*tiny_files)
+    g = torch.Generator().manual_seed(100 + n)
+    T = 5
+    toks = torch.randint(0, 4096, (T, n), generator=g).int()
+    outs = []
+    for mdl in (tc_model, simt_model):
+        k, v = mdl.new_batch_cache(n)
+        for t in range(T):
+            lg, am = mdl.forward_batch(toks[t].cuda(), torch.full((n,), t, dtype=torch.int32).cuda(), k, v,
+                                       argmax=True)
+        outs.append((lg.cpu(), am.cpu(), k[:, :, :T].cpu(), v[:, :, :T].cpu()))
+    (a_lg, a_am, a_k, a_v), (b_lg, b_am, b_k, b_v) = outs
+    assert float((a_lg - b_lg).abs().max()) <= LOGIT_TOL
+    assert float((a_k - b_k).abs().max()) <= 1e-4 and float((a_v - b_v).abs().max()) <= 1e-4
+    assert torch.equal(a_am.long(), a_lg.argmax(1))
+    orc = OracleModel.from_q6w(*tiny_files)
+    for i in (0, n // 2, n - 1):
+        ko, vo = orc.new_cache()
+        with torch.inference_mode():
+            for t in range(T):
+                want = orc.step(int(toks[t, i]), t, ko, vo)
+        assert float((a_lg[i] - want).abs().max()) <= LOGIT_TOL

@@ -17,12 +17,13 @@
 // sequence and feeds the next token; the whole step is captured once into a
 // CUDA graph and replayed, so the host never synchronises inside a request.
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <new>
 #include <vector>
 
-#include "linear.cuh"
+#include "tc.cuh"
 
 namespace q6w {
 
@@ -38,6 +39,9 @@ struct Work {
   int32_t* gen;
   int32_t* flags;
   int32_t* err;
+  uint8_t* xs_img;   // tensor-core path: activation images (see tc.cuh)
+  uint8_t* att_img;
+  uint8_t* hs_img;
 };
 
 struct GraphKey {
@@ -58,6 +62,8 @@ struct q6w_model {
   cudaGraphExec_t exec = nullptr;
   q6w::GraphKey key;
   bool have_key = false;
+  bool use_tc = false;  // shapes qualify for the tensor-core batched path
+  int sm_count = 148;
 };
 
 namespace q6w {
@@ -83,6 +89,13 @@ static size_t layout(const q6w_model* M, int N, char* base, Work* w) {
   t.plen = (int32_t*)carve(p, 4 * (size_t)N);
   t.gen = (int32_t*)carve(p, 4 * (size_t)N);
   t.flags = (int32_t*)carve(p, 4 * (size_t)N);
+  if (M->use_tc) {
+    t.xs_img = (uint8_t*)carve(p, tc::img_bytes(N, d.dim));
+    t.att_img = (uint8_t*)carve(p, tc::img_bytes(N, d.dim));
+    t.hs_img = (uint8_t*)carve(p, tc::img_bytes(N, d.hidden_dim));
+  } else {
+    t.xs_img = t.att_img = t.hs_img = nullptr;
+  }
   if (w) *w = t;
   return (size_t)(p - base);
 }
@@ -255,6 +268,199 @@ __global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb,
   }
 }
 
+// Decode attention, streaming form: one CTA (4 warps) per sequence reads that
+// sequence's K and V rows 0..T-1 exactly once -- a row holds all kv heads
+// (KV*HD floats, contiguous), so a warp covers 32/R consecutive rows with
+// R = KV*HD/16 lanes each, 16 dims per lane.  Every lane keeps an online
+// softmax state (max, sum, 16-dim accumulator) for each of the REP query
+// heads that share its kv head; states merge across lanes (shuffles) and
+// warps (shared memory) at the end and the output is acc / sum.  Same math
+// as torch_benchmark.py:117-119 with the softmax normalisation folded into
+// one final divide.
+template <int HD, int KV, int REP, bool SPLIT>
+__global__ void __launch_bounds__(128, 4) attn_rows_kernel(
+    const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+    int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
+    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom,
+    uint8_t* __restrict__ out_img) {
+  constexpr int C = HD / 16;  // 16-dim chunks per head
+  constexpr int R = KV * C;   // lanes per cached row
+  constexpr int PPW = 32 / R; // rows per warp pass
+  constexpr int NW = 4;
+  constexpr int PPC = PPW * NW;
+  static_assert(32 % R == 0, "a row must map onto a power-of-two lane group");
+  __shared__ float sm_m[NW][R][REP], sm_l[NW][R][REP];
+  __shared__ float4 sm_acc[NW][R][REP][4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x;
+  const int r = lane % R, kvh = r / C, chunk = r % C;
+  int T = len[b] + len_add;
+  T = T > S ? S : T;
+  float* ob = SPLIT ? nullptr : out + (int64_t)b * ldo;
+  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
+    if (SPLIT) {
+      const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int k = threadIdx.x * 8; k < KV * REP * HD; k += blockDim.x * 8) tc::img_store8(out_img, b, k, KV * REP * HD, z);
+    } else {
+      for (int i = threadIdx.x; i < KV * REP * HD; i += blockDim.x) ob[i] = 0.0f;
+    }
+    return;
+  }
+  float q[REP][16];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    const float4* qp = reinterpret_cast<const float4*>(qb + (int64_t)b * ldq + (kvh * REP + j) * HD + chunk * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = qp[i];
+      q[j][4 * i] = v.x; q[j][4 * i + 1] = v.y; q[j][4 * i + 2] = v.z; q[j][4 * i + 3] = v.w;
+    }
+  }
+  float m[REP], l[REP], acc[REP][16];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[j][i] = 0.0f;
+  }
+  const float* kb = kc + b * cstride + layer_off + r * 16;
+  const float* vb = vc + b * cstride + layer_off + r * 16;
+  for (int t0 = warp * PPW; t0 < T; t0 += PPC) {  // warp-uniform trip count
+    const int t = t0 + lane / R;
+    const bool act = t < T;
+    float kv[16], vv[16];
+    if (act) {
+      const float4* kp = reinterpret_cast<const float4*>(kb + (int64_t)t * (KV * HD));
+      const float4* vp = reinterpret_cast<const float4*>(vb + (int64_t)t * (KV * HD));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = kp[i], c = vp[i];
+        kv[4 * i] = a.x; kv[4 * i + 1] = a.y; kv[4 * i + 2] = a.z; kv[4 * i + 3] = a.w;
+        vv[4 * i] = c.x; vv[4 * i + 1] = c.y; vv[4 * i + 2] = c.z; vv[4 * i + 3] = c.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) kv[i] = vv[i] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < REP; ++j) {
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) d = fmaf(q[j][i], kv[i], d);
+#pragma unroll
+      for (int o = 1; o < C; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      if (act) {
+        const float sc = __fdiv_rn(d, denom);
+        if (sc > m[j]) {
+          const float c = expf(m[j] - sc);
+          l[j] *= c;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[j][i] *= c;
+          m[j] = sc;
+        }
+        const float p = expf(sc - m[j]);
+        l[j] += p;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[j][i] = fmaf(p, vv[i], acc[j][i]);
+      }
+    }
+  }
+  // merge the lanes of this warp that hold the same (kv head, chunk)
+#pragma unroll
+  for (int o = R; o < 32; o <<= 1) {
+#pragma unroll
+    for (int j = 0; j < REP; ++j) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[j], o);
+      const float lo = __shfl_xor_sync(0xffffffffu, l[j], o);
+      const float mt = fmaxf(m[j], mo);
+      const float ca = m[j] == -INFINITY ? 0.0f : expf(m[j] - mt);
+      const float cb = mo == -INFINITY ? 0.0f : expf(mo - mt);
+      l[j] = l[j] * ca + lo * cb;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float ao = __shfl_xor_sync(0xffffffffu, acc[j][i], o);
+        acc[j][i] = acc[j][i] * ca + ao * cb;
+      }
+      m[j] = mt;
+    }
+  }
+  if (lane < R) {
+#pragma unroll
+    for (int j = 0; j < REP; ++j) {
+      sm_m[warp][r][j] = m[j];
+      sm_l[warp][r][j] = l[j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        sm_acc[warp][r][j][i] = make_float4(acc[j][4 * i], acc[j][4 * i + 1], acc[j][4 * i + 2], acc[j][4 * i + 3]);
+    }
+  }
+  __syncthreads();
+  if (warp == 0 && lane < R) {
+#pragma unroll
+    for (int j = 0; j < REP; ++j) {
+      float mt = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) mt = fmaxf(mt, sm_m[w][r][j]);
+      float lt = 0.0f, o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float mw = sm_m[w][r][j];
+        const float c = mw == -INFINITY ? 0.0f : expf(mw - mt);
+        lt += sm_l[w][r][j] * c;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 a = sm_acc[w][r][j][i];
+          o[4 * i] += a.x * c; o[4 * i + 1] += a.y * c; o[4 * i + 2] += a.z * c; o[4 * i + 3] += a.w * c;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = __fdiv_rn(o[i], lt);
+      const int k0 = (kvh * REP + j) * HD + chunk * 16;
+      if (SPLIT) {
+        const float o0[8] = {o[0], o[1], o[2], o[3], o[4], o[5], o[6], o[7]};
+        const float o1[8] = {o[8], o[9], o[10], o[11], o[12], o[13], o[14], o[15]};
+        tc::img_store8(out_img, b, k0, KV * REP * HD, o0);
+        tc::img_store8(out_img, b, k0 + 8, KV * REP * HD, o1);
+      } else {
+        float4* op = reinterpret_cast<float4*>(ob + k0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) op[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      }
+    }
+  }
+}
+
+// Launch the streaming kernel when the shape has an instantiation; returns
+// false to fall back to the per-head kernel.
+static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st, const float* qb, int ldq,
+                             const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
+                             const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo,
+                             int S, float denom, uint8_t* out_img = nullptr) {
+#define Q6W_ROWS(HDV, KVV, REPV)                                                                          \
+  if (hd == HDV && KV == KVV && rep == REPV) {                                                            \
+    if (out_img)                                                                                          \
+      attn_rows_kernel<HDV, KVV, REPV, true><<<grid.x, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,  \
+                                                                     len, len_add, flags, out, ldo, S,    \
+                                                                     denom, out_img);                     \
+    else                                                                                                  \
+      attn_rows_kernel<HDV, KVV, REPV, false><<<grid.x, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off, \
+                                                                      len, len_add, flags, out, ldo, S,   \
+                                                                      denom, nullptr);                    \
+    return true;                                                                                          \
+  }
+  Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)
+  Q6W_ROWS(16, 1, 2) Q6W_ROWS(16, 2, 2) Q6W_ROWS(16, 4, 2) Q6W_ROWS(16, 8, 2)
+  Q6W_ROWS(16, 1, 4) Q6W_ROWS(16, 2, 4) Q6W_ROWS(16, 4, 4) Q6W_ROWS(16, 8, 4)
+  Q6W_ROWS(32, 1, 1) Q6W_ROWS(32, 2, 1) Q6W_ROWS(32, 4, 1)
+  Q6W_ROWS(32, 1, 2) Q6W_ROWS(32, 2, 2) Q6W_ROWS(32, 4, 2)
+  Q6W_ROWS(32, 1, 4) Q6W_ROWS(32, 2, 4) Q6W_ROWS(32, 4, 4)
+#undef Q6W_ROWS
+  return false;
+}
+
 struct StopSet {
   int32_t n, min_new;
   int32_t ids[kMaxStop];
@@ -310,8 +516,13 @@ __global__ void keys_to_argmax_kernel(int n, unsigned long long* keys, int32_t* 
 
 // ---- step enqueue --------------------------------------------------------------
 
+static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
+                               const EpiArgs& vocab_ep, cudaStream_t st);
+static int tc_min_seqs();
+
 static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc, float* vc,
                             int64_t cstride, const EpiArgs& vocab_ep, cudaStream_t st) {
+  if (M->use_tc && n >= tc_min_seqs()) return enqueue_step_tc(M, n, w, kc, vc, cstride, vocab_ep, st);
   const q6w_model_desc& d = M->d;
   const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
   embed_kernel<<<n < 2048 ? n : 2048, 128, 0, st>>>(d.tok_embeddings.packed,
@@ -347,6 +558,10 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
       e = LinearLauncher<true, EPI_QKV>::run(w.x, dim, n, L.attention_norm, d.norm_eps, ms, q, st);
       if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "qkv linear: %s", cudaGetErrorString(e));
     }
+    if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
+                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom)) {
+      Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    } else {
     switch (M->hd) {
 #define Q6W_ATTN(HDV)                                                                          \
   case HDV:                                                                                    \
@@ -361,6 +576,7 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
         return fail(Q6W_ERR_ARG, "unsupported head_dim %d", M->hd);
     }
     Q6W_LAUNCH_CHECK("attn_kernel");
+    }
     {
       MatSet ms = {L.wo.packed, nullptr, nullptr, L.wo.scales, nullptr, nullptr,
                    dim, dim, dim, 0, dim / 2};
@@ -401,6 +617,188 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
   cudaError_t e = LinearLauncher<true, EPI_VOCAB>::run(w.x, dim, n, d.norm, d.norm_eps, mv, v, st);
   if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "vocab linear: %s", cudaGetErrorString(e));
   return Q6W_OK;
+}
+
+// Tensor-core path: x[b] = dequant(E[token]) and the layer-0 activation image
+// of RMSNorm(x) * attention_norm[0] (torch_benchmark.py:97, 104).  Sixteen
+// lanes per sequence, eight values each (dim 128).
+__global__ void embed_tc_kernel(const uint8_t* __restrict__ E, const float* __restrict__ Es, int vocab,
+                                int max_seq, int n, Work w, const float* __restrict__ g, float eps) {
+  const int gl = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = gl >> 4, l = gl & 15;
+  const bool inb = b < n;
+  const int t = inb ? w.tok[b] : 0, p = inb ? w.pos[b] : 0;
+  const bool ok = inb && t >= 0 && t < vocab && p >= 0 && p < max_seq;
+  if (inb && l == 0) {
+    const int f = w.flags[b];
+    w.flags[b] = ok ? (f & ~SEQ_INVALID) : (f | SEQ_INVALID);
+    if (!ok && !(f & SEQ_DONE)) atomicOr(w.err, 1);
+  }
+  float v[8];
+  if (ok) {
+    const uint8_t* row = E + (int64_t)t * 96 + l * 6;
+    const float s = __ldg(Es + t);
+    const uint32_t g0 = load_group(row), g1 = load_group(row + 3);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = __fmul_rn((float)group_code(g0, i), s);
+      v[4 + i] = __fmul_rn((float)group_code(g1, i), s);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!inb) return;
+  float4* xr = reinterpret_cast<float4*>(w.x + (int64_t)b * 128 + l * 8);
+  xr[0] = make_float4(v[0], v[1], v[2], v[3]);
+  xr[1] = make_float4(v[4], v[5], v[6], v[7]);
+  const float r = rms_scale(ss, 128, eps);
+  float u[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) u[i] = __fmul_rn(__fmul_rn(v[i], r), __ldg(g + l * 8 + i));
+  tc::img_store8(w.xs_img, b, l * 8, 128, u);
+}
+
+static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st) {
+  const int items = ((a.n + tc::kM - 1) / tc::kM) * a.n_tiles;
+  const int grid = items < sms ? items : sms;
+  const size_t smem = tc::smem_bytes();
+  switch (epi) {
+    case tc::TEPI_QKV: tc::tc_gemm_kernel<tc::TEPI_QKV><<<grid, tc::kThreads, smem, st>>>(a); break;
+    case tc::TEPI_RESNORM: tc::tc_gemm_kernel<tc::TEPI_RESNORM><<<grid, tc::kThreads, smem, st>>>(a); break;
+    case tc::TEPI_GLU: tc::tc_gemm_kernel<tc::TEPI_GLU><<<grid, tc::kThreads, smem, st>>>(a); break;
+    default: tc::tc_gemm_kernel<tc::TEPI_VOCAB><<<grid, tc::kThreads, smem, st>>>(a); break;
+  }
+  Q6W_LAUNCH_CHECK("tc_gemm_kernel");
+  return Q6W_OK;
+}
+
+static int32_t tc_set_attrs() {
+  const int smem = (int)tc::smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_RESNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_VOCAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tensor-core kernel attributes: %s", cudaGetErrorString(e));
+  return Q6W_OK;
+}
+
+// The batched step on tensor cores (same kernels sequence and semantics as
+// enqueue_step; RMSNorm moves from the linear prologues into the epilogues
+// that produce each linear's input).
+static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
+                               const EpiArgs& vocab_ep, cudaStream_t st) {
+  const q6w_model_desc& d = M->d;
+  const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
+  embed_tc_kernel<<<(n * 16 + 127) / 128, 128, 0, st>>>(d.tok_embeddings.packed, d.tok_embeddings.scales,
+                                                        d.vocab_size, S, n, w, M->layers[0].attention_norm,
+                                                        d.norm_eps);
+  Q6W_LAUNCH_CHECK("embed_tc_kernel");
+  tc::TcArgs base;
+  memset(&base, 0, sizeof(base));
+  base.n = n;
+  base.err = w.err;
+  base.eps = d.norm_eps;
+  base.ep.pos = w.pos;
+  base.ep.flags = w.flags;
+  int32_t rc;
+  for (int l = 0; l < d.n_layers; ++l) {
+    const q6w_layer_weights& L = M->layers[l];
+    const int64_t layer_off = (int64_t)l * S * kvr;
+    {
+      tc::TcArgs a = base;
+      a.a_img = w.xs_img;
+      a.K = dim;
+      a.q0 = L.wq.packed; a.q1 = L.wk.packed; a.q2 = L.wv.packed;
+      a.s0 = L.wq.scales; a.s1 = L.wk.scales; a.s2 = L.wv.scales;
+      a.end0 = dim; a.end1 = dim + kvr;
+      a.N = dim + 2 * kvr;
+      a.n_tiles = 1;
+      a.ep.qbuf = w.qb; a.ep.ldq = dim;
+      a.ep.kc = kc; a.ep.vc = vc; a.ep.cache_stride = cstride; a.ep.layer_off = layer_off;
+      a.ep.rope_cos = d.rope_cos; a.ep.rope_sin = d.rope_sin;
+      a.ep.hd = M->hd; a.ep.q_rows = dim; a.ep.kv_rows = kvr;
+      if ((rc = tc_launch(tc::TEPI_QKV, a, M->sm_count, st))) return rc;
+    }
+    if (!launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, dim3(n), st, w.qb, dim, kc, vc,
+                          cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img))
+      return fail(Q6W_ERR_ARG, "no attention kernel for this head layout");
+    Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    {
+      tc::TcArgs a = base;
+      a.a_img = w.att_img;
+      a.K = dim;
+      a.q0 = L.wo.packed; a.s0 = L.wo.scales;
+      a.end0 = a.end1 = dim;
+      a.N = dim;
+      a.n_tiles = 1;
+      a.x = w.x; a.gnorm = L.ffn_norm; a.out_img = w.xs_img; a.out_K = dim;
+      if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st))) return rc;
+    }
+    {
+      tc::TcArgs a = base;
+      a.a_img = w.xs_img;
+      a.K = dim;
+      a.q0 = L.w1.packed; a.s0 = L.w1.scales; a.q1 = L.w3.packed; a.s1 = L.w3.scales;
+      a.N = 256;
+      a.n_tiles = hid / 128;
+      a.out_img = w.hs_img; a.out_K = hid;
+      if ((rc = tc_launch(tc::TEPI_GLU, a, M->sm_count, st))) return rc;
+    }
+    {
+      tc::TcArgs a = base;
+      a.a_img = w.hs_img;
+      a.K = hid;
+      a.q0 = L.w2.packed; a.s0 = L.w2.scales;
+      a.end0 = a.end1 = dim;
+      a.N = dim;
+      a.n_tiles = 1;
+      a.x = w.x;
+      a.gnorm = l + 1 < d.n_layers ? M->layers[l + 1].attention_norm : d.norm;
+      a.out_img = w.xs_img; a.out_K = dim;
+      if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st))) return rc;
+    }
+  }
+  tc::TcArgs a = base;
+  a.a_img = w.xs_img;
+  a.K = dim;
+  a.q0 = d.tok_embeddings.packed; a.s0 = d.tok_embeddings.scales;
+  a.end0 = a.end1 = d.vocab_size;
+  a.N = 256;
+  a.n_tiles = d.vocab_size / 256;
+  a.ep = vocab_ep;
+  a.ep.pos = w.pos;
+  a.ep.flags = w.flags;
+  a.ep.keys = w.keys;
+  a.ep.gen = w.gen;
+  a.ep.plen = w.plen;
+  a.ep.vocab = d.vocab_size;
+  return tc_launch(tc::TEPI_VOCAB, a, M->sm_count, st);
+}
+
+// Shapes the tensor-core step handles: dim 128, [wq|wk|wv] one N tile of at
+// most 256 rows in 32-row chunks, hidden a multiple of 128, vocab a multiple
+// of 256, and an instantiated streaming-attention layout.
+static bool tc_shapes_ok(const q6w_model_desc& d, int hd, int kvr) {
+  const int rep = d.n_heads / d.n_kv_heads;
+  return d.dim == 128 && kvr % 32 == 0 && d.dim + 2 * kvr <= 256 && d.hidden_dim % 128 == 0 &&
+         d.hidden_dim <= 1024 && d.vocab_size % 256 == 0 && (hd == 16 || hd == 32) && rep <= 4 &&
+         d.n_kv_heads * hd / 16 <= 32;
+}
+
+static int tc_min_seqs() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q6W_TC_MIN_SEQS");
+    v = e ? atoi(e) : 64;
+    if (v < 1) v = 1;
+  }
+  return v;
 }
 
 static int32_t check_qmat(const q6w_qmat& m, int rows, int cols, const char* name) {
@@ -486,6 +884,18 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
   if ((st = set_attn_attrs(M))) {
     delete M;
     return st;
+  }
+  cudaDeviceGetAttribute(&M->sm_count, cudaDevAttrMultiProcessorCount, M->device);
+  if (M->sm_count <= 0) M->sm_count = 148;
+  {
+    const char* off = getenv("Q6W_DISABLE_TC");
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, M->device);
+    M->use_tc = !(off && off[0] == '1') && major == 10 && tc_shapes_ok(d, hd, kvr);
+    if (M->use_tc && (st = tc_set_attrs())) {
+      delete M;
+      return st;
+    }
   }
   *out = M;
   return Q6W_OK;
@@ -733,6 +1143,11 @@ extern "C" int32_t q6w_gqa_attention(const float* queries, const float* keys, co
   const float denom = (float)sqrt((double)head_dim);
   cudaStream_t s = (cudaStream_t)stream;
   const int ld = H * head_dim;
+  if (launch_attn_rows(head_dim, kv_heads, groups_per_kv, grid, s, queries, ld, keys, values, kv_seq_stride, 0,
+                       lengths, 0, nullptr, output, ld, max_len, denom)) {
+    Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    return Q6W_OK;
+  }
   switch (head_dim) {
 #define Q6W_ATTN2(HDV)                                                                               \
   case HDV:                                                                                          \

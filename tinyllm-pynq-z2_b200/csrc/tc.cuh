@@ -1,0 +1,473 @@
+// Tensor-core (tcgen05) path for the batched step: n >= 64 sequences of a
+// model with dim 128.
+//
+// GEMM shape per CTA: D[128 sequences, N weight rows] += A[128, K] . B[N, K]^T
+// with A = activations, B = Q6W weights, both bf16 K-major in shared memory
+// with the 128-byte swizzle, D in FP32 in tensor memory (TMEM).
+//
+// Exactness.  A Q6W code is an integer in [-32, 31]: exact in bf16.  An FP32
+// activation u is carried as three bf16 parts u = hi + mid + lo (each part the
+// bf16 rounding of what the previous parts left; together they hold u's 24-bit
+// significand), so sum_k q_k u_k is formed from exact products with FP32
+// accumulation -- three MMAs per K step instead of one.  The row scale is
+// applied once in the epilogue: y = scale * sum_k q_k u_k.
+//
+// Activation images.  Producers (embed, attention, the wo / w2 / W1-W3
+// epilogues) write the next GEMM's A operand directly as a pre-swizzled tile
+// image: for 128-row tile t, part p, 64-column chunk c, row r, the 128 bytes
+// of the row are eight 16-byte units stored at unit index (u ^ (r & 7)) --
+// the byte image of the UMMA K-major SWIZZLE_128B canonical layout -- so a
+// CTA copies a whole A tile into shared memory with contiguous vector loads.
+//
+// Weights are expanded from the packed int6 rows into the same layout in
+// shared memory by the CTA itself (three 32-bit loads -> 16 bf16 codes).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "linear.cuh"
+
+namespace q6w {
+namespace tc {
+
+constexpr int kM = 128;             // sequences per tile (MMA M, TMEM lanes)
+constexpr int kKC = 128;            // K per shared-memory stage
+constexpr int kThreads = 128;       // 4 warps; thread i owns TMEM lane / sequence row i
+constexpr uint64_t kWaitCycles = 4000000000ull;  // bounded waits (~2 s)
+constexpr int kErrTimeout = 4;      // workspace error bit: an MMA wait timed out
+
+// ---- image addressing ---------------------------------------------------------
+
+// Byte offset, inside an activation image of K columns, of element (row, part, k).
+__host__ __device__ __forceinline__ int64_t img_offset(int64_t row, int part, int k, int K) {
+  const int64_t tile = row >> 7;
+  const int r = (int)(row & 127);
+  const int c = k >> 6, u = (k & 63) >> 3;
+  return tile * (3 * (int64_t)K * 256) + (int64_t)part * K * 256 + (int64_t)c * 16384 + r * 128 +
+         ((u ^ (r & 7)) << 4) + ((k & 7) << 1);
+}
+
+__host__ __device__ inline size_t img_bytes(int64_t n, int K) {
+  return (size_t)((n + 127) / 128) * 3 * (size_t)K * 256;
+}
+
+__device__ __forceinline__ uint32_t bf16_bits_rn(float x) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// u -> (hi, mid, lo) bf16 bit patterns, each the rounding of the remainder.
+__device__ __forceinline__ void split3(float u, uint32_t& h, uint32_t& m, uint32_t& l) {
+  h = bf16_bits_rn(u);
+  const float r1 = __fsub_rn(u, __uint_as_float(h << 16));
+  m = bf16_bits_rn(r1);
+  const float r2 = __fsub_rn(r1, __uint_as_float(m << 16));
+  l = bf16_bits_rn(r2);
+}
+
+// Write 8 consecutive values (k0 % 8 == 0) of one row into an image as three
+// 16-byte stores.
+__device__ __forceinline__ void img_store8(uint8_t* img, int64_t row, int k0, int K, const float (&v)[8]) {
+  uint32_t h[4], m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t h0, m0, l0, h1, m1, l1;
+    split3(v[2 * i], h0, m0, l0);
+    split3(v[2 * i + 1], h1, m1, l1);
+    h[i] = h0 | (h1 << 16);
+    m[i] = m0 | (m1 << 16);
+    l[i] = l0 | (l1 << 16);
+  }
+  const int64_t off = img_offset(row, 0, k0, K);
+  const int64_t ps = (int64_t)K * 256;
+  *reinterpret_cast<uint4*>(img + off) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(img + off + ps) = make_uint4(m[0], m[1], m[2], m[3]);
+  *reinterpret_cast<uint4*>(img + off + 2 * ps) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// ---- PTX wrappers --------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase; false if it did not complete in time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B
+// apart (stride byte offset), tile bases 1024-byte aligned.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: A and B bf16, D f32, both K-major, M=128.
+__host__ __device__ constexpr uint32_t idesc_bf16(int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive FP32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- GEMM --------------------------------------------------------------------
+
+enum { TEPI_QKV = 0, TEPI_RESNORM = 1, TEPI_GLU = 2, TEPI_VOCAB = 3 };
+
+struct TcArgs {
+  const uint8_t* a_img;  // activation image [ceil(n/128) tiles][3][K]
+  int32_t n, K;
+  // weights: B tile rows come from up to three matrices (see row_src)
+  const uint8_t* q0;
+  const uint8_t* q1;
+  const uint8_t* q2;
+  const float* s0;
+  const float* s1;
+  const float* s2;
+  int32_t end0, end1;  // QKV: virtual-row ends of wq and wk
+  int32_t N;           // rows per N tile (128 or 256)
+  int32_t n_tiles;     // N tiles per M tile
+  // epilogue
+  float* x;            // RESNORM: residual stream [n, 128] (read + written)
+  const float* gnorm;  // RESNORM: norm weight applied to the new x for the next image
+  float eps;
+  uint8_t* out_img;    // RESNORM / GLU: next GEMM's activation image
+  int32_t out_K;       // its K
+  EpiArgs ep;          // QKV / VOCAB fields (pos, flags, caches, rope, keys, stop set, logits)
+  int32_t* err;
+};
+
+// Source of B-tile row j of N tile `nt`: pointer to its packed row and scale.
+__device__ __forceinline__ void row_src(const TcArgs& a, int epi, int nt, int j, const uint8_t*& row,
+                                        float& sc) {
+  const int64_t rb = (int64_t)a.K * 3 / 4;
+  int r;
+  const uint8_t* q;
+  const float* s;
+  if (epi == TEPI_GLU) {  // rows 0..127: W1 rows 128nt.., rows 128..255: W3 rows 128nt..
+    r = nt * 128 + (j & 127);
+    q = j < 128 ? a.q0 : a.q1;
+    s = j < 128 ? a.s0 : a.s1;
+  } else {
+    const int v = nt * a.N + j;
+    if (v < a.end0) {
+      q = a.q0; s = a.s0; r = v;
+    } else if (v < a.end1) {
+      q = a.q1; s = a.s1; r = v - a.end0;
+    } else {
+      q = a.q2; s = a.s2; r = v - a.end1;
+    }
+  }
+  row = q + r * rb;
+  sc = __ldg(s + r);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t mma_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ float sscale[256];
+  __shared__ int timed_out;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;                  // [3][2][128][128 B] = 96 KB (one K stage)
+  uint8_t* sB = smem + 3 * kM * kKC * 2;  // [2][N][128 B]
+
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&mma_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    timed_out = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = tmem_base;
+  const uint32_t idesc = idesc_bf16(a.N);
+  const int m_tiles = (a.n + kM - 1) / kM;
+  const int items = m_tiles * a.n_tiles;
+  const int per = (items + gridDim.x - 1) / gridDim.x;
+  const int it0 = blockIdx.x * per, it1 = min(items, it0 + per);
+  uint32_t phase = 0;
+  int loaded_m = -1;
+  const int kstages = a.K / kKC;
+
+  for (int it = it0; it < it1 && !timed_out; ++it) {
+    const int mt = it / a.n_tiles, nt = it % a.n_tiles;
+    for (int ks = 0; ks < kstages; ++ks) {
+      // A stage: 3 parts x 128 rows x 128 columns, a contiguous copy per part
+      if (mt != loaded_m || kstages > 1) {
+        const uint8_t* src = a.a_img + (int64_t)mt * 3 * a.K * 256 + (int64_t)ks * 32768;
+        for (int i = tid; i < 3 * 2048; i += kThreads) {  // 16-byte units
+          const int p = i >> 11, u = i & 2047;
+          reinterpret_cast<uint4*>(sA + p * 32768)[u] =
+              __ldg(reinterpret_cast<const uint4*>(src + (int64_t)p * a.K * 256) + u);
+        }
+        loaded_m = mt;
+      }
+      // B stage: expand N rows x 128 codes to bf16
+      for (int i = tid; i < a.N * 8; i += kThreads) {
+        const int j = i >> 3, u = i & 7;  // row j, 16-code unit u
+        const uint8_t* row;
+        float sc;
+        row_src(a, EPI, nt, j, row, sc);
+        if (u == 0 && ks == 0) sscale[j] = sc;
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(row + (ks * 8 + u) * 12);
+        const uint32_t w0 = __ldg(pw), w1 = __ldg(pw + 1), w2 = __ldg(pw + 2);
+        uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
+                          w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
+                          w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          pk[e] = (__float_as_uint(code_to_float(f[2 * e])) >> 16) |
+                  (__float_as_uint(code_to_float(f[2 * e + 1])) & 0xFFFF0000u);
+        const int c64 = u >> 2, lu = (u & 3) * 2;
+        uint8_t* line = sB + c64 * (a.N * 128) + j * 128;
+        reinterpret_cast<uint4*>(line)[lu ^ (j & 7)] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        reinterpret_cast<uint4*>(line)[(lu + 1) ^ (j & 7)] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+#pragma unroll 1
+        for (int p = 0; p < 3; ++p)
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sdesc(a0 + p * 32768 + c * 16384 + kk * 32);
+              const uint64_t bd = sdesc(b0 + c * (a.N * 128) + kk * 32);
+              umma(taddr, ad, bd, idesc, (ks | p | c | kk) != 0);
+            }
+        umma_commit(&mma_bar);
+      }
+      if (!mbar_wait(&mma_bar, phase)) {
+        if (tid == 0) atomicOr(a.err, kErrTimeout);
+        timed_out = 1;
+      }
+      phase ^= 1;
+      tc_fence_after();
+      __syncthreads();
+      if (timed_out) break;
+    }
+    if (timed_out) break;
+
+    // ---- epilogue: thread tid owns sequence m
+    const int64_t m = (int64_t)mt * kM + tid;
+    const bool live = m < a.n;
+    const uint32_t lane_addr = taddr + ((uint32_t)(warp * 32) << 16);
+    if (EPI == TEPI_VOCAB) {
+      const EpiArgs& ep = a.ep;
+      unsigned long long best = 0ull;
+      const bool mask = live && ep.n_stop && ep.gen[m] < ep.min_new;
+      const bool dump = live && ep.step_logits && !(ep.flags[m] & (SEQ_DONE | SEQ_INVALID)) &&
+                        ep.pos[m] >= ep.plen[m] - 1;
+      for (int c0 = 0; c0 < a.N; c0 += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + c0, v);
+        if (!live) continue;
+        const int r0 = nt * a.N + c0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], sscale[c0 + i]);
+        if (ep.y) {
+          float4* y = reinterpret_cast<float4*>(ep.y + m * ep.ldy + r0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+        if (dump) {
+          float4* y = reinterpret_cast<float4*>(ep.step_logits + (m * ep.new_tokens + ep.gen[m]) * ep.vocab + r0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float val = v[i];
+          if (mask)
+            for (int s = 0; s < ep.n_stop; ++s)
+              if (ep.stop_ids[s] == r0 + i) val = -INFINITY;
+          best = umax64(best, argmax_key(val, r0 + i));
+        }
+      }
+      if (live) atomicMax(ep.keys + m, best);
+    } else if (EPI == TEPI_QKV) {
+      const EpiArgs& ep = a.ep;
+      const bool ok = live && !(ep.flags[m] & SEQ_INVALID);
+      const int pos = ok ? ep.pos[m] : 0;
+      for (int c0 = 0; c0 < a.N; c0 += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + c0, v);
+        if (!ok) continue;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], sscale[c0 + i]);
+        const int v0 = nt * a.N + c0;  // first virtual row of this chunk
+        if (v0 < ep.q_rows + ep.kv_rows) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int j = ((v0 + i) % ep.hd) >> 1;
+            const float cs = __ldg(ep.rope_cos + (int64_t)pos * (ep.hd >> 1) + j);
+            const float sn = __ldg(ep.rope_sin + (int64_t)pos * (ep.hd >> 1) + j);
+            const float ra = __fsub_rn(__fmul_rn(v[i], cs), __fmul_rn(v[i + 1], sn));
+            const float rb = __fadd_rn(__fmul_rn(v[i], sn), __fmul_rn(v[i + 1], cs));
+            v[i] = ra;
+            v[i + 1] = rb;
+          }
+        }
+        float* dst;
+        if (v0 < ep.q_rows)
+          dst = ep.qbuf + m * ep.ldq + v0;
+        else if (v0 < ep.q_rows + ep.kv_rows)
+          dst = ep.kc + m * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v0 - ep.q_rows);
+        else
+          dst = ep.vc + m * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
+                (v0 - ep.q_rows - ep.kv_rows);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim
+      float xn[128];
+      float ss = 0.0f;
+#pragma unroll
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + c0, v);
+        if (live) {
+          const float4* xr = reinterpret_cast<const float4*>(a.x + m * 128 + c0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 o = xr[i];
+            xn[c0 + 4 * i] = __fadd_rn(o.x, __fmul_rn(v[4 * i], sscale[c0 + 4 * i]));
+            xn[c0 + 4 * i + 1] = __fadd_rn(o.y, __fmul_rn(v[4 * i + 1], sscale[c0 + 4 * i + 1]));
+            xn[c0 + 4 * i + 2] = __fadd_rn(o.z, __fmul_rn(v[4 * i + 2], sscale[c0 + 4 * i + 2]));
+            xn[c0 + 4 * i + 3] = __fadd_rn(o.w, __fmul_rn(v[4 * i + 3], sscale[c0 + 4 * i + 3]));
+          }
+        }
+      }
+      if (live) {
+        float4* xw = reinterpret_cast<float4*>(a.x + m * 128);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          xw[i] = make_float4(xn[4 * i], xn[4 * i + 1], xn[4 * i + 2], xn[4 * i + 3]);
+          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i], xn[4 * i]));
+          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + 1], xn[4 * i + 1]));
+          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + 2], xn[4 * i + 2]));
+          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + 3], xn[4 * i + 3]));
+        }
+        const float rstd = rms_scale(ss, 128, a.eps);
+#pragma unroll
+        for (int k0 = 0; k0 < 128; k0 += 8) {
+          float u8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) u8[i] = __fmul_rn(__fmul_rn(xn[k0 + i], rstd), __ldg(a.gnorm + k0 + i));
+          img_store8(a.out_img, m, k0, 128, u8);
+        }
+      }
+    } else if (EPI == TEPI_GLU) {  // N == 256: columns j (W1) and 128 + j (W3)
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float va[32], vb[32];
+        tmem_ld32(lane_addr + c0, va);
+        tmem_ld32(lane_addr + 128 + c0, vb);
+        if (!live) continue;
+#pragma unroll
+        for (int k0 = 0; k0 < 32; k0 += 8) {
+          float h8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            h8[i] = swiglu(__fmul_rn(va[k0 + i], sscale[c0 + k0 + i]), __fmul_rn(vb[k0 + i], sscale[128 + c0 + k0 + i]));
+          img_store8(a.out_img, m, nt * 128 + c0 + k0, a.out_K, h8);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(taddr, 256);
+  }
+}
+
+constexpr size_t smem_bytes() { return 1024 + 3 * kM * kKC * 2 + 256 * kKC * 2; }
+
+}  // namespace tc
+}  // namespace q6w
