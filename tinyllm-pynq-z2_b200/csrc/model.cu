@@ -268,41 +268,34 @@ __global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb,
   }
 }
 
-// Decode attention, streaming form: one CTA (4 warps) per sequence reads that
-// sequence's K and V rows 0..T-1 exactly once -- a row holds all kv heads
-// (KV*HD floats, contiguous), so a warp covers 32/R consecutive rows with
-// R = KV*HD/16 lanes each, 16 dims per lane.  Every lane keeps an online
-// softmax state (max, sum, 16-dim accumulator) for each of the REP query
-// heads that share its kv head; states merge across lanes (shuffles) and
-// warps (shared memory) at the end and the output is acc / sum.  Same math
-// as torch_benchmark.py:117-119 with the softmax normalisation folded into
-// one final divide.
+// Decode attention, one warp per sequence: the warp streams the sequence's
+// K and V rows 0..T-1 once (32/R rows per pass, R = KV*HD/16 lanes per row,
+// 16 dims per lane), prefetching the next pass's rows while it computes the
+// current one, with an online softmax per lane for the REP query heads of
+// its kv head; lanes holding the same (kv head, dims) merge by shuffles.
 template <int HD, int KV, int REP, bool SPLIT>
-__global__ void __launch_bounds__(128, 4) attn_rows_kernel(
+__global__ void __launch_bounds__(128) attn_warp_kernel(
     const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
-    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom,
+    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom, int n,
     uint8_t* __restrict__ out_img) {
-  constexpr int C = HD / 16;  // 16-dim chunks per head
-  constexpr int R = KV * C;   // lanes per cached row
-  constexpr int PPW = 32 / R; // rows per warp pass
-  constexpr int NW = 4;
-  constexpr int PPC = PPW * NW;
+  constexpr int C = HD / 16;
+  constexpr int R = KV * C;
+  constexpr int PPW = 32 / R;
+  constexpr int ROW = KV * HD;  // floats per cached row
   static_assert(32 % R == 0, "a row must map onto a power-of-two lane group");
-  __shared__ float sm_m[NW][R][REP], sm_l[NW][R][REP];
-  __shared__ float4 sm_acc[NW][R][REP][4];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= n) return;
   const int r = lane % R, kvh = r / C, chunk = r % C;
   int T = len[b] + len_add;
   T = T > S ? S : T;
-  float* ob = SPLIT ? nullptr : out + (int64_t)b * ldo;
   if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
     if (SPLIT) {
       const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int k = threadIdx.x * 8; k < KV * REP * HD; k += blockDim.x * 8) tc::img_store8(out_img, b, k, KV * REP * HD, z);
+      for (int k = lane * 8; k < KV * REP * HD; k += 256) tc::img_store8(out_img, b, k, KV * REP * HD, z);
     } else {
-      for (int i = threadIdx.x; i < KV * REP * HD; i += blockDim.x) ob[i] = 0.0f;
+      for (int i = lane; i < KV * REP * HD; i += 32) out[(int64_t)b * ldo + i] = 0.0f;
     }
     return;
   }
@@ -324,24 +317,33 @@ __global__ void __launch_bounds__(128, 4) attn_rows_kernel(
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[j][i] = 0.0f;
   }
-  const float* kb = kc + b * cstride + layer_off + r * 16;
-  const float* vb = vc + b * cstride + layer_off + r * 16;
-  for (int t0 = warp * PPW; t0 < T; t0 += PPC) {  // warp-uniform trip count
-    const int t = t0 + lane / R;
+  const float4* kb = reinterpret_cast<const float4*>(kc + b * cstride + layer_off + r * 16);
+  const float4* vb = reinterpret_cast<const float4*>(vc + b * cstride + layer_off + r * 16);
+  const int t_lane = lane / R;
+  float4 kn[4], vn[4];
+  {
+    const bool act = t_lane < T;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      kn[i] = act ? kb[(int64_t)t_lane * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      vn[i] = act ? vb[(int64_t)t_lane * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  for (int t0 = 0; t0 < T; t0 += PPW) {
+    const int t = t0 + t_lane;
     const bool act = t < T;
     float kv[16], vv[16];
-    if (act) {
-      const float4* kp = reinterpret_cast<const float4*>(kb + (int64_t)t * (KV * HD));
-      const float4* vp = reinterpret_cast<const float4*>(vb + (int64_t)t * (KV * HD));
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 a = kp[i], c = vp[i];
-        kv[4 * i] = a.x; kv[4 * i + 1] = a.y; kv[4 * i + 2] = a.z; kv[4 * i + 3] = a.w;
-        vv[4 * i] = c.x; vv[4 * i + 1] = c.y; vv[4 * i + 2] = c.z; vv[4 * i + 3] = c.w;
-      }
-    } else {
+    for (int i = 0; i < 4; ++i) {
+      kv[4 * i] = kn[i].x; kv[4 * i + 1] = kn[i].y; kv[4 * i + 2] = kn[i].z; kv[4 * i + 3] = kn[i].w;
+      vv[4 * i] = vn[i].x; vv[4 * i + 1] = vn[i].y; vv[4 * i + 2] = vn[i].z; vv[4 * i + 3] = vn[i].w;
+    }
+    const int tn = t + PPW;
+    const bool actn = tn < T;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) kv[i] = vv[i] = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+      kn[i] = actn ? kb[(int64_t)tn * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      vn[i] = actn ? vb[(int64_t)tn * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int j = 0; j < REP; ++j) {
@@ -366,7 +368,6 @@ __global__ void __launch_bounds__(128, 4) attn_rows_kernel(
       }
     }
   }
-  // merge the lanes of this warp that hold the same (kv head, chunk)
 #pragma unroll
   for (int o = R; o < 32; o <<= 1) {
 #pragma unroll
@@ -388,36 +389,9 @@ __global__ void __launch_bounds__(128, 4) attn_rows_kernel(
   if (lane < R) {
 #pragma unroll
     for (int j = 0; j < REP; ++j) {
-      sm_m[warp][r][j] = m[j];
-      sm_l[warp][r][j] = l[j];
+      float o[16];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        sm_acc[warp][r][j][i] = make_float4(acc[j][4 * i], acc[j][4 * i + 1], acc[j][4 * i + 2], acc[j][4 * i + 3]);
-    }
-  }
-  __syncthreads();
-  if (warp == 0 && lane < R) {
-#pragma unroll
-    for (int j = 0; j < REP; ++j) {
-      float mt = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) mt = fmaxf(mt, sm_m[w][r][j]);
-      float lt = 0.0f, o[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = 0.0f;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float mw = sm_m[w][r][j];
-        const float c = mw == -INFINITY ? 0.0f : expf(mw - mt);
-        lt += sm_l[w][r][j] * c;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 a = sm_acc[w][r][j][i];
-          o[4 * i] += a.x * c; o[4 * i + 1] += a.y * c; o[4 * i + 2] += a.z * c; o[4 * i + 3] += a.w * c;
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = __fdiv_rn(o[i], lt);
+      for (int i = 0; i < 16; ++i) o[i] = __fdiv_rn(acc[j][i], l[j]);
       const int k0 = (kvh * REP + j) * HD + chunk * 16;
       if (SPLIT) {
         const float o0[8] = {o[0], o[1], o[2], o[3], o[4], o[5], o[6], o[7]};
@@ -425,7 +399,7 @@ __global__ void __launch_bounds__(128, 4) attn_rows_kernel(
         tc::img_store8(out_img, b, k0, KV * REP * HD, o0);
         tc::img_store8(out_img, b, k0 + 8, KV * REP * HD, o1);
       } else {
-        float4* op = reinterpret_cast<float4*>(ob + k0);
+        float4* op = reinterpret_cast<float4*>(out + (int64_t)b * ldo + k0);
 #pragma unroll
         for (int i = 0; i < 4; ++i) op[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
       }
@@ -441,14 +415,15 @@ static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st
                              int S, float denom, uint8_t* out_img = nullptr) {
 #define Q6W_ROWS(HDV, KVV, REPV)                                                                          \
   if (hd == HDV && KV == KVV && rep == REPV) {                                                            \
+    const int nb = ((int)grid.x + 3) / 4;                                                                 \
     if (out_img)                                                                                          \
-      attn_rows_kernel<HDV, KVV, REPV, true><<<grid.x, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,  \
-                                                                     len, len_add, flags, out, ldo, S,    \
-                                                                     denom, out_img);                     \
+      attn_warp_kernel<HDV, KVV, REPV, true><<<nb, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,      \
+                                                                 len, len_add, flags, out, ldo, S,        \
+                                                                 denom, (int)grid.x, out_img);            \
     else                                                                                                  \
-      attn_rows_kernel<HDV, KVV, REPV, false><<<grid.x, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off, \
-                                                                      len, len_add, flags, out, ldo, S,   \
-                                                                      denom, nullptr);                    \
+      attn_warp_kernel<HDV, KVV, REPV, false><<<nb, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,     \
+                                                                  len, len_add, flags, out, ldo, S,       \
+                                                                  denom, (int)grid.x, nullptr);           \
     return true;                                                                                          \
   }
   Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)

@@ -115,6 +115,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Bulk (non-tensor, non-multicast) global -> shared copy completing on `bar`;
+// addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
                "r"(ncols)
@@ -207,42 +221,73 @@ struct TcArgs {
   int32_t* err;
 };
 
-// Source of B-tile row j of N tile `nt`: pointer to its packed row and scale.
-__device__ __forceinline__ void row_src(const TcArgs& a, int epi, int nt, int j, const uint8_t*& row,
-                                        float& sc) {
-  const int64_t rb = (int64_t)a.K * 3 / 4;
-  int r;
+// The B tile of N tile `nt` as up to three contiguous row segments of the
+// weight matrices (rows of one segment are consecutive in the file image):
+// QKV: wq | wk | wv; GLU: W1 rows 128nt.. | W3 rows 128nt..; otherwise one.
+struct Seg {
   const uint8_t* q;
   const float* s;
-  if (epi == TEPI_GLU) {  // rows 0..127: W1 rows 128nt.., rows 128..255: W3 rows 128nt..
-    r = nt * 128 + (j & 127);
-    q = j < 128 ? a.q0 : a.q1;
-    s = j < 128 ? a.s0 : a.s1;
-  } else {
-    const int v = nt * a.N + j;
-    if (v < a.end0) {
-      q = a.q0; s = a.s0; r = v;
-    } else if (v < a.end1) {
-      q = a.q1; s = a.s1; r = v - a.end0;
-    } else {
-      q = a.q2; s = a.s2; r = v - a.end1;
+  int r0, rows;
+};
+
+__device__ __forceinline__ int b_segments(const TcArgs& a, int epi, int nt, Seg (&sg)[3]) {
+  if (epi == TEPI_GLU) {
+    sg[0] = {a.q0, a.s0, nt * 128, 128};
+    sg[1] = {a.q1, a.s1, nt * 128, 128};
+    return 2;
+  }
+  if (epi == TEPI_QKV) {
+    sg[0] = {a.q0, a.s0, 0, a.end0};
+    sg[1] = {a.q1, a.s1, 0, a.end1 - a.end0};
+    sg[2] = {a.q2, a.s2, 0, a.N - a.end1};
+    return 3;
+  }
+  sg[0] = {a.q0, a.s0, nt * a.N, a.N};
+  return 1;
+}
+
+// Thread 0: start the bulk copies of stage `ks` of item (mt, nt): the A
+// stage when `want_a`, the packed B rows (all K) and their scales when
+// `want_b`; all complete on `bar`.
+__device__ __forceinline__ void issue_loads(const TcArgs& a, int epi, int mt, int nt, int ks, bool want_a,
+                                            bool want_b, uint8_t* sA, uint8_t* stage, uint64_t* bar) {
+  const uint32_t rb = (uint32_t)a.K * 3 / 4;
+  Seg sg[3];
+  const int nseg = b_segments(a, epi, nt, sg);
+  uint32_t bytes = want_a ? 3 * 32768 : 0;
+  if (want_b) bytes += (uint32_t)a.N * (rb + 4);
+  mbar_expect_tx(bar, bytes);
+  if (want_a) {
+    const uint8_t* src = a.a_img + (int64_t)mt * 3 * a.K * 256 + (int64_t)ks * 32768;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) bulk_g2s(sA + p * 32768, src + (int64_t)p * a.K * 256, 32768, bar);
+  }
+  if (want_b) {
+    uint8_t* dst = stage;
+    float* sdst = reinterpret_cast<float*>(stage + (size_t)a.N * rb);
+    for (int i = 0; i < nseg; ++i) {
+      bulk_g2s(dst, sg[i].q + (int64_t)sg[i].r0 * rb, (uint32_t)sg[i].rows * rb, bar);
+      bulk_g2s(sdst, sg[i].s + sg[i].r0, (uint32_t)sg[i].rows * 4, bar);
+      dst += (size_t)sg[i].rows * rb;
+      sdst += sg[i].rows;
     }
   }
-  row = q + r * rb;
-  sc = __ldg(s + r);
 }
+
+// Shared memory: [A stage 96 KB][B tile N x 128 bf16, 64 KB][packed B rows + scales, <= 37 KB]
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t mma_bar;
+  __shared__ uint64_t mma_bar, ld_bar;
   __shared__ uint32_t tmem_base;
   __shared__ float sscale[256];
   __shared__ int timed_out;
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = smem;                  // [3][2][128][128 B] = 96 KB (one K stage)
-  uint8_t* sB = smem + 3 * kM * kKC * 2;  // [2][N][128 B]
+  uint8_t* sA = smem;                       // [3][2][128][128 B] = 96 KB (one K stage)
+  uint8_t* sB = smem + 3 * kM * kKC * 2;    // [2][N][128 B]
+  uint8_t* stage = sB + 256 * kKC * 2;      // packed rows [N][K*3/4] + scales [N]
 
   if (warp == 0) {
     tmem_alloc(&tmem_base, 256);
@@ -250,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   }
   if (tid == 0) {
     mbar_init(&mma_bar, 1);
+    mbar_init(&ld_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     timed_out = 0;
   }
@@ -262,35 +308,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   const int items = m_tiles * a.n_tiles;
   const int per = (items + gridDim.x - 1) / gridDim.x;
   const int it0 = blockIdx.x * per, it1 = min(items, it0 + per);
-  uint32_t phase = 0;
-  int loaded_m = -1;
   const int kstages = a.K / kKC;
+  const uint32_t rb = (uint32_t)a.K * 3 / 4;
+  uint32_t ph_mma = 0, ph_ld = 0;
+  if (tid == 0 && it0 < it1) issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 0, true, true, sA, stage, &ld_bar);
 
   for (int it = it0; it < it1 && !timed_out; ++it) {
     const int mt = it / a.n_tiles, nt = it % a.n_tiles;
     for (int ks = 0; ks < kstages; ++ks) {
-      // A stage: 3 parts x 128 rows x 128 columns, a contiguous copy per part
-      if (mt != loaded_m || kstages > 1) {
-        const uint8_t* src = a.a_img + (int64_t)mt * 3 * a.K * 256 + (int64_t)ks * 32768;
-        for (int i = tid; i < 3 * 2048; i += kThreads) {  // 16-byte units
-          const int p = i >> 11, u = i & 2047;
-          reinterpret_cast<uint4*>(sA + p * 32768)[u] =
-              __ldg(reinterpret_cast<const uint4*>(src + (int64_t)p * a.K * 256) + u);
-        }
-        loaded_m = mt;
+      if (!mbar_wait(&ld_bar, ph_ld)) {
+        if (tid == 0) atomicOr(a.err, kErrTimeout);
+        timed_out = 1;
       }
-      // B stage: expand N rows x 128 codes to bf16
+      ph_ld ^= 1;
+      __syncthreads();
+      if (timed_out) break;
+      // expand N rows x 128 codes (columns 128ks..) from the staged bytes to bf16
+      if (ks == 0)
+        for (int j = tid; j < a.N; j += kThreads)
+          sscale[j] = reinterpret_cast<const float*>(stage + (size_t)a.N * rb)[j];
       for (int i = tid; i < a.N * 8; i += kThreads) {
-        const int j = i >> 3, u = i & 7;  // row j, 16-code unit u
-        const uint8_t* row;
-        float sc;
-        row_src(a, EPI, nt, j, row, sc);
-        if (u == 0 && ks == 0) sscale[j] = sc;
-        const uint32_t* pw = reinterpret_cast<const uint32_t*>(row + (ks * 8 + u) * 12);
-        const uint32_t w0 = __ldg(pw), w1 = __ldg(pw + 1), w2 = __ldg(pw + 2);
-        uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
-                          w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
-                          w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
+        const int j = i >> 3, u = i & 7;
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(stage + j * rb + (ks * 8 + u) * 12);
+        const uint32_t w0 = pw[0], w1 = pw[1], w2 = pw[2];
+        const uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
+                                w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
+                                w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e)
@@ -318,12 +361,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
             }
         umma_commit(&mma_bar);
       }
-      if (!mbar_wait(&mma_bar, phase)) {
+      if (!mbar_wait(&mma_bar, ph_mma)) {
         if (tid == 0) atomicOr(a.err, kErrTimeout);
         timed_out = 1;
       }
-      phase ^= 1;
+      ph_mma ^= 1;
       tc_fence_after();
+      // prefetch the next stage / item while this one's epilogue runs
+      if (tid == 0 && !timed_out) {
+        if (ks + 1 < kstages) {
+          issue_loads(a, EPI, mt, nt, ks + 1, true, false, sA, stage, &ld_bar);
+        } else if (it + 1 < it1) {
+          const int mt2 = (it + 1) / a.n_tiles;
+          issue_loads(a, EPI, mt2, (it + 1) % a.n_tiles, 0, mt2 != mt || kstages > 1, true, sA, stage, &ld_bar);
+        }
+      }
       __syncthreads();
       if (timed_out) break;
     }
@@ -467,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   }
 }
 
-constexpr size_t smem_bytes() { return 1024 + 3 * kM * kKC * 2 + 256 * kKC * 2; }
+constexpr size_t smem_bytes() { return 1024 + 3 * kM * kKC * 2 + 256 * kKC * 2 + 128 * (288 + 4); }
 
 }  // namespace tc
 }  // namespace q6w
