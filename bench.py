@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--cpu-sample-requests", type=int, default=2, help="requests per CPU worker per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-main", action="store_true", help="skip the B=1, GEMV and CPU side measurements")
     return ap.parse_args()
 
 
@@ -293,8 +294,8 @@ def run_b200(a):
 
     # ---- dominant kernel alone: decode attention over this run's caches
     roof = attention_roofline(model, caches, n, P + T - 1, stream)
-    b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if rank == 0 else None
-    gemv = scaled_gemv(dev, stream) if rank == 0 else None
+    b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if rank == 0 and not a.only_main else None
+    gemv = scaled_gemv(dev, stream) if rank == 0 and not a.only_main else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -316,7 +317,7 @@ def run_b200(a):
             "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len,
             "b1": b1, "gemv_scaled": gemv,
         }
-        if not a.no_cpu_baseline and world == 1:
+        if not a.no_cpu_baseline and not a.only_main and world == 1:
             cores = cpu_cores()
             rows = host_prompts[: 4 * cores].tolist()
             v, toks, busy, wall = cpu_throughput(b, m, rows, T, cores, a.cpu_sample_requests)

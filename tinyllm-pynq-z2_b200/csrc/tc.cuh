@@ -32,7 +32,7 @@ namespace tc {
 
 constexpr int kM = 128;             // sequences per tile (MMA M, TMEM lanes)
 constexpr int kKC = 128;            // K per shared-memory stage
-constexpr int kThreads = 128;       // 4 warps; thread i owns TMEM lane / sequence row i
+constexpr int kThreads = 256;       // 8 warps; warps w and w+4 share TMEM lanes 32(w%4).. (sequence rows), splitting the columns
 constexpr uint64_t kWaitCycles = 4000000000ull;  // bounded waits (~2 s)
 constexpr int kErrTimeout = 4;      // workspace error bit: an MMA wait timed out
 
@@ -281,7 +281,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t mma_bar, ld_bar;
   __shared__ uint32_t tmem_base;
-  __shared__ float sscale[256];
+  __shared__ __align__(16) float sscale[256];
+  __shared__ float ss_part[2][kM];
   __shared__ int timed_out;
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -381,23 +382,35 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
     }
     if (timed_out) break;
 
-    // ---- epilogue: thread tid owns sequence m
-    const int64_t m = (int64_t)mt * kM + tid;
+    // ---- epilogue: lane quadrant q = warp & 3 holds sequence rows 32q..32q+31
+    // (TMEM lanes); warps q and q + 4 take the two halves of the columns.
+    const int row = ((warp & 3) << 5) | (tid & 31);
+    const int half = warp >> 2;
+    const int64_t m = (int64_t)mt * kM + row;
     const bool live = m < a.n;
-    const uint32_t lane_addr = taddr + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_addr = taddr + ((uint32_t)((warp & 3) * 32) << 16);
     if (EPI == TEPI_VOCAB) {
       const EpiArgs& ep = a.ep;
-      unsigned long long best = 0ull;
       const bool mask = live && ep.n_stop && ep.gen[m] < ep.min_new;
       const bool dump = live && ep.step_logits && !(ep.flags[m] & (SEQ_DONE | SEQ_INVALID)) &&
                         ep.pos[m] >= ep.plen[m] - 1;
-      for (int c0 = 0; c0 < a.N; c0 += 32) {
+      float bv = -INFINITY;
+      int bi = -1;
+      const int cb = half * (a.N >> 1), ce = cb + (a.N >> 1);
+      for (int c0 = cb; c0 < ce; c0 += 32) {
         float v[32];
         tmem_ld32(lane_addr + c0, v);
         if (!live) continue;
         const int r0 = nt * a.N + c0;
+        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], sscale[c0 + i]);
+        for (int i = 0; i < 8; ++i) {
+          const float4 sc = s4[i];
+          v[4 * i] = __fmul_rn(v[4 * i], sc.x);
+          v[4 * i + 1] = __fmul_rn(v[4 * i + 1], sc.y);
+          v[4 * i + 2] = __fmul_rn(v[4 * i + 2], sc.z);
+          v[4 * i + 3] = __fmul_rn(v[4 * i + 3], sc.w);
+        }
         if (ep.y) {
           float4* y = reinterpret_cast<float4*>(ep.y + m * ep.ldy + r0);
 #pragma unroll
@@ -408,35 +421,63 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
         }
+        if (mask) {
+          for (int s = 0; s < ep.n_stop; ++s) {
+            const int k = ep.stop_ids[s] - r0;
+            if (k >= 0 && k < 32) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float val = v[i];
-          if (mask)
-            for (int s = 0; s < ep.n_stop; ++s)
-              if (ep.stop_ids[s] == r0 + i) val = -INFINITY;
-          best = umax64(best, argmax_key(val, r0 + i));
+              for (int i = 0; i < 32; ++i)
+                if (i == k) v[i] = -INFINITY;
+            }
+          }
         }
+        // first maximum in increasing column order (torch.argmax's tie rule)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (v[i] > bv || bi < 0) {
+            bv = v[i];
+            bi = r0 + i;
+          }
       }
-      if (live) atomicMax(ep.keys + m, best);
+      if (live && bi >= 0) atomicMax(ep.keys + m, argmax_key(bv, bi));
     } else if (EPI == TEPI_QKV) {
       const EpiArgs& ep = a.ep;
       const bool ok = live && !(ep.flags[m] & SEQ_INVALID);
       const int pos = ok ? ep.pos[m] : 0;
-      for (int c0 = 0; c0 < a.N; c0 += 32) {
+      const int hh = ep.hd >> 1;  // 8 or 16 rotation frequencies
+      float cs[16], sn[16];
+      if (ok) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          cs[i] = i < hh ? __ldg(ep.rope_cos + (int64_t)pos * hh + i) : 0.0f;
+          sn[i] = i < hh ? __ldg(ep.rope_sin + (int64_t)pos * hh + i) : 0.0f;
+        }
+      }
+      const int cb = half * (a.N >> 1), ce = cb + (a.N >> 1);
+      for (int c0 = cb; c0 < ce; c0 += 32) {
         float v[32];
         tmem_ld32(lane_addr + c0, v);
         if (!ok) continue;
+        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], sscale[c0 + i]);
+        for (int i = 0; i < 8; ++i) {
+          const float4 sc = s4[i];
+          v[4 * i] = __fmul_rn(v[4 * i], sc.x);
+          v[4 * i + 1] = __fmul_rn(v[4 * i + 1], sc.y);
+          v[4 * i + 2] = __fmul_rn(v[4 * i + 2], sc.z);
+          v[4 * i + 3] = __fmul_rn(v[4 * i + 3], sc.w);
+        }
         const int v0 = nt * a.N + c0;  // first virtual row of this chunk
         if (v0 < ep.q_rows + ep.kv_rows) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const int j = ((v0 + i) % ep.hd) >> 1;
-            const float cs = __ldg(ep.rope_cos + (int64_t)pos * (ep.hd >> 1) + j);
-            const float sn = __ldg(ep.rope_sin + (int64_t)pos * (ep.hd >> 1) + j);
-            const float ra = __fsub_rn(__fmul_rn(v[i], cs), __fmul_rn(v[i + 1], sn));
-            const float rb = __fadd_rn(__fmul_rn(v[i], sn), __fmul_rn(v[i + 1], cs));
+            const int j = ((v0 + i) & (ep.hd - 1)) >> 1;
+            float c = cs[0], sv = sn[0];
+#pragma unroll
+            for (int f = 1; f < 16; ++f)
+              if (f == j) { c = cs[f]; sv = sn[f]; }
+            const float ra = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + 1], sv));
+            const float rb = __fadd_rn(__fmul_rn(v[i], sv), __fmul_rn(v[i + 1], c));
             v[i] = ra;
             v[i + 1] = rb;
           }
@@ -453,47 +494,54 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
-    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim
-      float xn[128];
+    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim; this thread: columns 64*half..+63
+      float xn[64];
       float ss = 0.0f;
 #pragma unroll
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int cc = 0; cc < 64; cc += 32) {
+        const int c0 = half * 64 + cc;
         float v[32];
         tmem_ld32(lane_addr + c0, v);
         if (live) {
           const float4* xr = reinterpret_cast<const float4*>(a.x + m * 128 + c0);
+          const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 o = xr[i];
-            xn[c0 + 4 * i] = __fadd_rn(o.x, __fmul_rn(v[4 * i], sscale[c0 + 4 * i]));
-            xn[c0 + 4 * i + 1] = __fadd_rn(o.y, __fmul_rn(v[4 * i + 1], sscale[c0 + 4 * i + 1]));
-            xn[c0 + 4 * i + 2] = __fadd_rn(o.z, __fmul_rn(v[4 * i + 2], sscale[c0 + 4 * i + 2]));
-            xn[c0 + 4 * i + 3] = __fadd_rn(o.w, __fmul_rn(v[4 * i + 3], sscale[c0 + 4 * i + 3]));
+            const float4 sc = s4[i];
+            xn[cc + 4 * i] = __fadd_rn(o.x, __fmul_rn(v[4 * i], sc.x));
+            xn[cc + 4 * i + 1] = __fadd_rn(o.y, __fmul_rn(v[4 * i + 1], sc.y));
+            xn[cc + 4 * i + 2] = __fadd_rn(o.z, __fmul_rn(v[4 * i + 2], sc.z));
+            xn[cc + 4 * i + 3] = __fadd_rn(o.w, __fmul_rn(v[4 * i + 3], sc.w));
           }
         }
       }
       if (live) {
-        float4* xw = reinterpret_cast<float4*>(a.x + m * 128);
+        float4* xw = reinterpret_cast<float4*>(a.x + m * 128 + half * 64);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           xw[i] = make_float4(xn[4 * i], xn[4 * i + 1], xn[4 * i + 2], xn[4 * i + 3]);
-          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i], xn[4 * i]));
-          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + 1], xn[4 * i + 1]));
-          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + 2], xn[4 * i + 2]));
-          ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + 3], xn[4 * i + 3]));
-        }
-        const float rstd = rms_scale(ss, 128, a.eps);
 #pragma unroll
-        for (int k0 = 0; k0 < 128; k0 += 8) {
-          float u8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) u8[i] = __fmul_rn(__fmul_rn(xn[k0 + i], rstd), __ldg(a.gnorm + k0 + i));
-          img_store8(a.out_img, m, k0, 128, u8);
+          for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + e], xn[4 * i + e]));
         }
       }
-    } else if (EPI == TEPI_GLU) {  // N == 256: columns j (W1) and 128 + j (W3)
+      ss_part[half][row] = ss;
+      __syncthreads();
+      if (live) {
+        const float rstd = rms_scale(__fadd_rn(ss_part[0][row], ss_part[1][row]), 128, a.eps);
+#pragma unroll
+        for (int k0 = 0; k0 < 64; k0 += 8) {
+          float u8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            u8[i] = __fmul_rn(__fmul_rn(xn[k0 + i], rstd), __ldg(a.gnorm + half * 64 + k0 + i));
+          img_store8(a.out_img, m, half * 64 + k0, 128, u8);
+        }
+      }
+    } else if (EPI == TEPI_GLU) {  // N == 256: columns j (W1) and 128 + j (W3); this thread: j in 64*half..
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int cc = 0; cc < 64; cc += 32) {
+        const int c0 = half * 64 + cc;
         float va[32], vb[32];
         tmem_ld32(lane_addr + c0, va);
         tmem_ld32(lane_addr + 128 + c0, vb);
