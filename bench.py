@@ -229,7 +229,8 @@ def run_b200(a):
     rank, world, local = dist_env()
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120))
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -450,9 +451,13 @@ def attention_roofline(model, caches, n, length, stream):
     nbytes = 2 * n * length * KV * hd * 4 + 2 * n * H * hd * 4
     peak, kind = measured_peaks()
     ach = nbytes / sec / 1e9
-    return {"kernel": "attn_kernel (decode GQA attention, timed alone)", "bound": "hbm", "achieved": round(ach, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": f"{kind} hbm_gbs",
-            "traffic": None, "bytes_per_launch": nbytes, "us_per_launch": round(sec * 1e6, 2)}
+    # DRAM bytes of one launch from ncu (profiles/attn_warp_tiny_2048seq_len147.md: 159.89 MB read +
+    # written at 2048 sequences, length 147), scaled by the sequence count
+    traffic = int(159.89e6 * n / 2048) if length == 147 else None
+    return {"kernel": "attn_warp_kernel (decode GQA attention, timed alone)", "bound": "hbm",
+            "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+            "peak_kind": f"{kind} hbm_gbs (copy, burst)", "traffic": traffic, "bytes_per_launch": nbytes,
+            "us_per_launch": round(sec * 1e6, 2)}
 
 
 def main():
