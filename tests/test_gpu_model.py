@@ -261,3 +261,50 @@ def test_tensor_core_step_matches_simt_step(tiny_files, monkeypatch, n):
             for t in range(T):
                 want = orc.step(int(toks[t, i]), t, ko, vo)
         assert float((a_lg[i] - want).abs().max()) <= LOGIT_TOL
+
+
+def test_b1_cluster_kernel_matches_graph_path(tiny_files, monkeypatch):
+    """Single requests run as one cluster kernel; compare with the per-step
+    CUDA-graph path on the same prompts (logits and KV caches) and verify the
+    tokens against the oracle by teacher forcing."""
+    fast = Q6WCudaTransformer.from_q6w(*tiny_files)
+    monkeypatch.setenv("Q6W_DISABLE_B1", "1")
+    graph = Q6WCudaTransformer.from_q6w(*tiny_files)
+    orc = OracleModel.from_q6w(*tiny_files)
+    prompts = _ragged_prompts(4, 21, 1, 60)
+    new = 40
+    picks = []
+    for p in prompts:
+        a = fast.generate_greedy([p], new, keep_logits=True)
+        b = graph.generate_greedy([p], new, keep_logits=True)
+        n = min(len(a.sampled[0]), len(b.sampled[0]))
+        assert float((a.logits[0, :n] - b.logits[0, :n]).abs().max()) <= LOGIT_TOL
+        T = len(p) + new - 1
+        ka, va = a.caches
+        kb, vb = b.caches
+        assert float((ka[0, :, :T] - kb[0, :, :T]).abs().max()) <= 1e-4
+        assert float((va[0, :, :T] - vb[0, :, :T]).abs().max()) <= 1e-4
+        picks.append(a.sampled[0])
+    summary = BatchScorer(orc).verify_greedy(prompts, picks, new)
+    assert summary["failures"] == []
+
+
+def test_b1_cluster_kernel_long_context(tmp_path_factory, monkeypatch):
+    """A single request past 256 positions (shipped shapes, 512-position
+    context): each thread of the cluster kernel's attention then holds two
+    positions."""
+    args = {"dim": 128, "n_layers": 5, "n_heads": 4, "n_kv_heads": 2, "vocab_size": 4096, "multiple_of": 32,
+            "max_seq_len": 512, "dropout": 0.0}
+    files = small_model_files(tmp_path_factory, args, 78, "longctx")
+    fast = Q6WCudaTransformer.from_q6w(*files)
+    monkeypatch.setenv("Q6W_DISABLE_B1", "1")
+    graph = Q6WCudaTransformer.from_q6w(*files)
+    orc = OracleModel.from_q6w(*files)
+    p = _ragged_prompts(1, 77, 200, 200)[0]
+    new = 300
+    a = fast.generate_greedy([p], new, keep_logits=True)
+    b = graph.generate_greedy([p], new, keep_logits=True)
+    n = min(len(a.sampled[0]), len(b.sampled[0]))
+    assert float((a.logits[0, :n] - b.logits[0, :n]).abs().max()) <= LOGIT_TOL
+    summary = BatchScorer(orc).verify_greedy([p], [a.sampled[0]], new)
+    assert summary["failures"] == []

@@ -23,6 +23,7 @@
 #include <new>
 #include <vector>
 
+#include "b1.cuh"
 #include "tc.cuh"
 
 namespace q6w {
@@ -64,6 +65,8 @@ struct q6w_model {
   bool have_key = false;
   bool use_tc = false;  // shapes qualify for the tensor-core batched path
   int sm_count = 148;
+  bool use_b1 = false;  // shapes qualify for the single-request cluster kernel
+  size_t b1_smem = 0;
 };
 
 namespace q6w {
@@ -807,6 +810,45 @@ static int32_t set_attn_attrs(const q6w_model* M) {
   return Q6W_OK;
 }
 
+static void b1_fill(const q6w_model* M, b1::Args& a) {
+  memset(&a, 0, sizeof(a));
+  const q6w_model_desc& d = M->d;
+  a.dim = d.dim; a.n_layers = d.n_layers; a.n_heads = d.n_heads; a.n_kv = d.n_kv_heads; a.hd = M->hd;
+  a.hidden = d.hidden_dim; a.vocab = d.vocab_size; a.max_seq = d.max_seq_len;
+  a.eps = d.norm_eps; a.denom = M->denom;
+  a.tok = {d.tok_embeddings.packed, d.tok_embeddings.scales};
+  a.norm = d.norm; a.rope_cos = d.rope_cos; a.rope_sin = d.rope_sin;
+  for (int l = 0; l < d.n_layers && l < b1::kMaxLayers; ++l) {
+    const q6w_layer_weights& L = M->layers[l];
+    a.layers[l].wq = {L.wq.packed, L.wq.scales}; a.layers[l].wk = {L.wk.packed, L.wk.scales};
+    a.layers[l].wv = {L.wv.packed, L.wv.scales}; a.layers[l].wo = {L.wo.packed, L.wo.scales};
+    a.layers[l].w1 = {L.w1.packed, L.w1.scales}; a.layers[l].w2 = {L.w2.packed, L.w2.scales};
+    a.layers[l].w3 = {L.w3.packed, L.w3.scales};
+    a.layers[l].attn_norm = L.attention_norm; a.layers[l].ffn_norm = L.ffn_norm;
+  }
+}
+
+// Shapes the cluster kernel handles: dim 128, at most 8 layers and 8 query
+// heads (one per CTA), head_dim 16 or 32, and every CTA's weight slice plus
+// vectors within 220 KB of shared memory.
+static bool b1_shapes_ok(const q6w_model* M, size_t* smem) {
+  const q6w_model_desc& d = M->d;
+  if (d.dim != 128 || d.n_layers > b1::kMaxLayers || d.n_heads > b1::kCtas || (M->hd != 16 && M->hd != 32) ||
+      d.hidden_dim % 16 || d.vocab_size % 16 || (d.dim + 2 * M->kv_rows) % 16 ||
+      d.hidden_dim < (b1::kThreads / 32) * M->hd)  // attention partials borrow the hidden vector
+    return false;
+  b1::Args a;
+  b1_fill(M, a);
+  size_t mx = 0;
+  for (int c = 0; c < b1::kCtas; ++c) {
+    b1::Plan p;
+    b1::make_plan(a, c, p);
+    mx = p.bytes > mx ? p.bytes : mx;
+  }
+  *smem = mx;
+  return mx <= b1::kMaxSmem;
+}
+
 }  // namespace q6w
 
 using namespace q6w;
@@ -870,6 +912,17 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
     if (M->use_tc && (st = tc_set_attrs())) {
       delete M;
       return st;
+    }
+    const char* off1 = getenv("Q6W_DISABLE_B1");
+    M->use_b1 = !(off1 && off1[0] == '1') && major == 10 && b1_shapes_ok(M, &M->b1_smem);
+    if (M->use_b1) {
+      // the attribute belongs to the function, not the model: allow the cap every model is held to
+      cudaError_t e = cudaFuncSetAttribute(b1::b1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)b1::kMaxSmem);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        M->use_b1 = false;  // the batched step still serves single requests
+      }
     }
   }
   *out = M;
@@ -1036,6 +1089,42 @@ extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, v
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != M->device) return fail(Q6W_ERR_ARG, "model was created on device %d, current is %d", M->device, dev);
+
+  if (n == 1 && M->use_b1) {  // one request: the cluster kernel runs the whole loop
+    cudaStream_t s = (cudaStream_t)stream;
+    b1::Args ba;
+    b1_fill(M, ba);
+    ba.prompt = a->prompts;
+    ba.prompt_len = a->prompt_lens;
+    ba.max_prompt_len = a->max_prompt_len;
+    ba.new_tokens = a->new_tokens;
+    ba.n_stop = stop.n;
+    ba.min_new = stop.min_new;
+    for (int i = 0; i < kMaxStop; ++i) ba.stop_ids[i] = stop.ids[i];
+    ba.kc = a->k_cache;
+    ba.vc = a->v_cache;
+    ba.sampled = a->sampled;
+    ba.n_sampled = a->n_sampled;
+    ba.stop_reason = a->stop_reason;
+    ba.step_logits = a->step_logits;
+    ba.state = reinterpret_cast<int32_t*>(w.x);  // 5 ints of the (unused) residual-stream row
+    ba.err = w.err;
+    b1::b1_init_kernel<<<1, 32, 0, s>>>(a->prompts, a->prompt_lens, a->max_prompt_len, M->d.vocab_size, ba.state,
+                                       a->n_sampled, a->stop_reason, w.err);
+    Q6W_LAUNCH_CHECK("b1_init_kernel");
+    const int total = a->max_prompt_len + a->new_tokens - 1;
+    const int cuts[3] = {0, a->max_prompt_len, total};
+    for (int part = 0; part < 2; ++part) {
+      if (cuts[part + 1] > cuts[part]) {
+        ba.step_begin = cuts[part];
+        ba.step_end = cuts[part + 1];
+        b1::b1_kernel<<<b1::kCtas, b1::kThreads, M->b1_smem, s>>>(ba);
+        Q6W_LAUNCH_CHECK("b1_kernel");
+      }
+      if (part == 0 && a->prefill_event) Q6W_CUDA_TRY(cudaEventRecord((cudaEvent_t)a->prefill_event, s));
+    }
+    return Q6W_OK;
+  }
 
   GraphKey key;
   memset(&key, 0, sizeof(key));
