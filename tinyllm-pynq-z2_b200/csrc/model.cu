@@ -829,13 +829,12 @@ static void b1_fill(const q6w_model* M, b1::Args& a) {
 }
 
 // Shapes the cluster kernel handles: dim 128, at most 8 layers and 8 query
-// heads (one per CTA), head_dim 16 or 32, and every CTA's weight slice plus
-// vectors within 220 KB of shared memory.
+// heads (one per CTA), head_dim 16 or 32, hidden and vocab multiples of 16,
+// and every CTA's weights plus vectors within the shared-memory cap.
 static bool b1_shapes_ok(const q6w_model* M, size_t* smem) {
   const q6w_model_desc& d = M->d;
   if (d.dim != 128 || d.n_layers > b1::kMaxLayers || d.n_heads > b1::kCtas || (M->hd != 16 && M->hd != 32) ||
-      d.hidden_dim % 16 || d.vocab_size % 16 || (d.dim + 2 * M->kv_rows) % 16 ||
-      d.hidden_dim < (b1::kThreads / 32) * M->hd)  // attention partials borrow the hidden vector
+      d.n_heads * M->hd != d.dim || d.n_heads % d.n_kv_heads || d.hidden_dim % 16 || d.vocab_size % 16)
     return false;
   b1::Args a;
   b1_fill(M, a);
