@@ -48,6 +48,27 @@ def test_linear_sweep(rows, cols, n):
     assert np.abs(y - ref32.numpy()).max() <= 1e-4
 
 
+# One activation row at K a multiple of 512 takes the HBM-streaming kernel
+# (bulk-copied tiles, factored row scale, 2^-p pre-scaled inputs): the
+# 1.1B-shape matrices and the extremes of its warp layout (K 512 / 4096).
+STREAM_SHAPES = [(2048, 2048), (256, 2048), (5632, 2048), (2048, 5632), (512, 512), (1024, 4096), (6016, 2048)]
+
+
+@pytest.mark.parametrize("rows,cols", STREAM_SHAPES)
+def test_linear_stream_one_row(rows, cols):
+    q, s, x, packed = make(rows, cols, 1, rows + 5 * cols)
+    y = ops.q6w_linear(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols).cpu().numpy()
+    check(y, q, s, x)
+
+
+def test_linear_stream_argmax():
+    q, s, x, packed = make(4096, 2048, 1, 4242)
+    am, lg = ops.linear_argmax(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), 4096, 2048, True)
+    lg = lg.cpu().numpy()
+    check(lg, q, s, x)
+    assert np.array_equal(am.cpu().numpy(), lg.argmax(axis=1))
+
+
 @pytest.mark.parametrize("rows,cols,n", [(63, 128, 3), (6, 20, 9), (10, 36, 1), (2, 4, 1), (4096, 128, 2)])
 def test_linear_general_shapes(rows, cols, n):
     q, s, x, packed = make(rows, cols, n, 11 + rows + cols + n)

@@ -205,6 +205,10 @@ def test_scaled_shapes_parity(tmp_path_factory):
             lg, _ = cuda.forward_batch(torch.full((n,), t, dtype=torch.int32).cuda(),
                                        torch.full((n,), p, dtype=torch.int32).cuda(), kb, vb)
         assert float((lg.cpu() - bb).abs().max()) <= LOGIT_TOL
+    # single-request device loop (streaming GEMVs in a captured graph), teacher-forced
+    res = cuda.generate_greedy([prompt], 12)
+    summary = BatchScorer(orc).verify_greedy([prompt], res.sampled, 12)
+    assert summary["failures"] == []
 
 
 def test_shipped_artifact_request(shipped_files_env, golden_shipped):

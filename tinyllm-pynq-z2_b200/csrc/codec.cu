@@ -23,6 +23,42 @@ int32_t fail(int32_t code, const char* fmt, ...) {
 
 void clear_error() { g_msg[0] = 0; }
 
+// Multiprocessor count of the current device (cached per device).
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+      cudaGetLastError();
+      v = 148;
+    }
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+namespace stream {
+// Bit 4 is set by a streaming-kernel wait that ran out of time (a
+// should-never-happen diagnostic; the kernel then skips the rest of its work).
+__device__ int32_t g_error_word;
+
+int32_t* error_word() {
+  static int32_t* cache[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) cudaGetLastError();
+    cache[dev] = static_cast<int32_t*>(p);
+  }
+  return cache[dev];
+}
+}  // namespace stream
+
 int grid_for(int64_t work, int threads) {
   static int sms = 0;
   if (!sms) {

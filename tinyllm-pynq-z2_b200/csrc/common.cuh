@@ -29,6 +29,11 @@ void clear_error();
                          cudaGetErrorString(e_));                                       \
   } while (0)
 
+int sm_count();
+namespace stream {
+int32_t* error_word();
+}
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // ---- Q6W decode --------------------------------------------------------------

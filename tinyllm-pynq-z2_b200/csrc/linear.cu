@@ -3,7 +3,7 @@
 
 #include <mutex>
 
-#include "linear.cuh"
+#include "launch.cuh"
 
 namespace q6w {
 

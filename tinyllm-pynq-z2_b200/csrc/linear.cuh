@@ -407,50 +407,4 @@ __global__ void __launch_bounds__(256) gemm_kernel(const float* __restrict__ x, 
   }
 }
 
-// Host launcher.  Chooses the kernel by n; returns a status.
-int grid_for(int64_t work, int threads);
-
-template <bool RMS, int EPI>
-struct LinearLauncher {
-  template <int NB, int G>
-  static cudaError_t gemv(const float* x, int ldx, int n, const float* g, float eps,
-                          const MatSet& ms, const EpiArgs& ep, cudaStream_t st) {
-    const int U = ms.cols >> 4;
-    const size_t smem = (size_t)NB * U * 64;
-    auto kern = gemv_kernel<NB, G, RMS, EPI>;
-    if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-    }
-    const int groups_per_cta = 8 * (32 / G);
-    int blocks = (ms.n_pairs + groups_per_cta - 1) / groups_per_cta;
-    if (blocks < 1) blocks = 1;
-    kern<<<blocks, 256, smem, st>>>(x, ldx, n, g, eps, ms, ep);
-    return cudaGetLastError();
-  }
-
-  template <int NB>
-  static cudaError_t gemv_g(const float* x, int ldx, int n, const float* g, float eps,
-                            const MatSet& ms, const EpiArgs& ep, cudaStream_t st) {
-    if ((ms.cols >> 4) >= 64) return gemv<NB, 32>(x, ldx, n, g, eps, ms, ep, st);
-    return gemv<NB, 8>(x, ldx, n, g, eps, ms, ep, st);
-  }
-
-  static cudaError_t run(const float* x, int ldx, int n, const float* g, float eps,
-                         const MatSet& ms, const EpiArgs& ep, cudaStream_t st) {
-    if (n <= 0 || ms.n_pairs <= 0) return cudaSuccess;
-    const int nb = n <= 2 ? n : (n <= 4 ? 4 : 8);
-    const bool small_ok = n <= 8 && (size_t)nb * ms.cols * sizeof(float) <= 200 * 1024;
-    if (!small_ok) {
-      dim3 grid((ms.n_pairs + 31) / 32, (n + 127) / 128);
-      gemm_kernel<RMS, EPI><<<grid, 256, 0, st>>>(x, ldx, n, g, eps, ms, ep);
-      return cudaGetLastError();
-    }
-    if (n == 1) return gemv_g<1>(x, ldx, n, g, eps, ms, ep, st);
-    if (n == 2) return gemv_g<2>(x, ldx, n, g, eps, ms, ep, st);
-    if (n <= 4) return gemv_g<4>(x, ldx, n, g, eps, ms, ep, st);
-    return gemv_g<8>(x, ldx, n, g, eps, ms, ep, st);
-  }
-};
-
 }  // namespace q6w

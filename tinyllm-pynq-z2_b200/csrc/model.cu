@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "b1.cuh"
+#include "launch.cuh"
 #include "tc.cuh"
 
 namespace q6w {

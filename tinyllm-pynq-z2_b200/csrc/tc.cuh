@@ -25,6 +25,7 @@
 
 #include <cuda_bf16.h>
 
+#include "async.cuh"
 #include "linear.cuh"
 
 namespace q6w {
@@ -33,7 +34,6 @@ namespace tc {
 constexpr int kM = 128;             // sequences per tile (MMA M, TMEM lanes)
 constexpr int kKC = 128;            // K per shared-memory stage
 constexpr int kThreads = 256;       // 8 warps; warps w and w+4 share TMEM lanes 32(w%4).. (sequence rows), splitting the columns
-constexpr uint64_t kWaitCycles = 4000000000ull;  // bounded waits (~2 s)
 constexpr int kErrTimeout = 4;      // workspace error bit: an MMA wait timed out
 
 // ---- image addressing ---------------------------------------------------------
@@ -84,50 +84,7 @@ __device__ __forceinline__ void img_store8(uint8_t* img, int64_t row, int k0, in
   *reinterpret_cast<uint4*>(img + off + 2 * ps) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// ---- PTX wrappers --------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait on an mbarrier phase; false if it did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-  return true;
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-// Bulk (non-tensor, non-multicast) global -> shared copy completing on `bar`;
-// addresses 16-byte aligned, size a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
+// ---- PTX wrappers (mbarrier and bulk-copy helpers are in async.cuh) ------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
