@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--cpu-sample-requests", type=int, default=2, help="requests per CPU worker per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-main", action="store_true", help="skip the B=1, GEMV and CPU side measurements")
+    ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
+                    help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
     return ap.parse_args()
 
 
@@ -297,6 +299,7 @@ def run_b200(a):
     roof = attention_roofline(model, caches, n, P + T - 1, stream)
     b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if rank == 0 and not a.only_main else None
     gemv = scaled_gemv(dev, stream) if rank == 0 and not a.only_main else None
+    sb1 = scaled_b1(dev, stream) if rank == 0 and not a.only_main else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -316,7 +319,7 @@ def run_b200(a):
                     "d2h_bytes_per_step": int(n * T * 4)},
             "gpu_launches": launches_per_gen * a.steps,
             "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len,
-            "b1": b1, "gemv_scaled": gemv,
+            "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1,
         }
         if not a.no_cpu_baseline and not a.only_main and world == 1:
             cores = cpu_cores()
@@ -413,11 +416,99 @@ def scaled_gemv(dev, stream, reps=10):
     moved = nbytes + sum(4 * (r + c) for r, c in shapes)
     peak, kind = measured_peaks()
     del g
+    # the largest matrix alone (vocab, 49 MB): four copies cycled, so each
+    # launch reads its weights from HBM (4 x 49 MB > the 126 MB L2)
+    vq, vs, vr, vc = mats[-1]
+    copies = [vq] + [torch.randint(0, 256, vq.shape, dtype=torch.uint8, device=dev) for _ in range(3)]
+    vy = torch.empty(vr, device=dev)
+    gv = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gv, stream=side):
+        h = _lib.stream_handle(side)
+        for k in range(4 * reps):
+            _lib.check(lib.q6w_linear(copies[k % 4].data_ptr(), vs.data_ptr(), x.data_ptr(), vy.data_ptr(), vr, vc, 1, h))
+    gv.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    gv.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    vsec = e0.elapsed_time(e1) / 1e3 / (4 * reps)
+    vbytes = vr * vc * 3 // 4 + 4 * vr + 4 * (vr + vc)
+    del gv, copies
     return {"workload": "B=1 Q6W GEMV pass over the 1.1B-shape matrices (155 launches, CUDA graph)",
             "bytes_per_token": moved, "us_per_token": round(sec * 1e6, 2),
             "achieved_gbs": round(moved / sec / 1e9, 1), "peak_gbs": peak,
             "frac": round(moved / sec / 1e9 / peak, 4), "peak_kind": f"{kind} hbm_gbs",
-            "weights_tok_s_ceiling": round(1 / sec, 1)}
+            "weights_tok_s_ceiling": round(1 / sec, 1),
+            "vocab_32000x2048": {"us_per_launch": round(vsec * 1e6, 2), "bytes": vbytes,
+                                 "achieved_gbs": round(vbytes / vsec / 1e9, 1),
+                                 "frac": round(vbytes / vsec / 1e9 / peak, 4)}}
+
+
+def scaled_b1(dev, stream, reps=3):
+    """B=1 greedy decode of the 1.1B-shape config (dim 2048, 22 layers, 32
+    heads / 4 kv heads, hidden 5632, vocab 32000): 128-token prompt + 128
+    tokens through the device loop (streaming GEMVs chained by programmatic
+    dependent launch inside the step graph).  Random 6-bit codes stand in
+    for trained weights (same bytes and shapes, so the same cost)."""
+    import torch
+
+    from q6w_b200 import format as fmt
+    from q6w_b200.model import Q6WCudaTransformer
+
+    args = dict(fmt.SCALED_ARGS)
+    model = Q6WCudaTransformer(fmt.RandomImage(args, seed=7), device=dev)
+    P, T = 128, 128
+    g = torch.Generator().manual_seed(11)
+    pr = torch.randint(3, args["vocab_size"], (1, P), generator=g, dtype=torch.int32).to(dev)
+    ln = torch.tensor([P], dtype=torch.int32, device=dev)
+    caches = model.new_batch_cache(1)
+    for _ in range(2):
+        model.generate_greedy_device(pr, ln, P, T, caches=caches)
+    torch.cuda.synchronize()
+    dec, tot = [], []
+    for _ in range(reps):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        model.generate_greedy_device(pr, ln, P, T, caches=caches, prefill_event=e1)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        tot.append(e0.elapsed_time(e2) / 1e3)
+        dec.append(e1.elapsed_time(e2) / 1e3)
+    d, t = statistics.median(dec), statistics.median(tot)
+    # decode steps: T - 1 model steps after the prefill part (P steps)
+    step_s = d / (T - 1)
+    wbytes = sum(e["data_bytes"] + e.get("scale_bytes", 0) for e in model.image.tensors.values())
+    peak, kind = measured_peaks()
+    del model, caches
+    torch.cuda.empty_cache()
+    return {"workload": "B=1 greedy, 1.1B-shape config, 128-token prompt + 128 tokens (random 6-bit codes)",
+            "decode_tok_s": round((T - 1) / d, 1), "request_tok_s": round(T / t, 1),
+            "us_per_model_step": round(step_s * 1e6, 2), "weight_bytes_per_step": wbytes,
+            "weights_gbs": round(wbytes / step_s / 1e9, 1), "frac_of_hbm": round(wbytes / step_s / 1e9 / peak, 4),
+            "peak_kind": f"{kind} hbm_gbs"}
+
+
+def profile_gemv(shape):
+    """One B=1 GEMV shape, 4 launches on random data: the small case the
+    ncu summaries under profiles/ are taken on."""
+    import torch
+
+    from q6w_b200 import _lib
+
+    rows, cols = (int(v) for v in shape.lower().split("x"))
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    lib = _lib.load()
+    q = torch.randint(0, 256, (rows * cols * 3 // 4,), dtype=torch.uint8, device=dev)
+    sc = torch.rand(rows, device=dev) * 0.05 + 0.001
+    x = torch.randn(cols, device=dev)
+    y = torch.empty(rows, device=dev)
+    h = _lib.stream_handle()
+    for _ in range(4):
+        _lib.check(lib.q6w_linear(q.data_ptr(), sc.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, 1, h))
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_gemv": shape, "launches": 4, "y_abs_sum": float(y.abs().sum())}), flush=True)
 
 
 def attention_roofline(model, caches, n, length, stream):
@@ -462,7 +553,9 @@ def attention_roofline(model, caches, n, length, stream):
 
 def main():
     a = parse()
-    if a.impl == "reference":
+    if a.profile_gemv:
+        profile_gemv(a.profile_gemv)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_b200(a)

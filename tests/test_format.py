@@ -114,3 +114,31 @@ def test_reader_detects_bad_shape(small):
 def test_reader_accepts_shipped_artifact(shipped_files):
     img = fmt.Q6WImage(*shipped_files)
     assert img.model_args["dim"] == 128 and len(img.tensors) == 47
+
+
+def test_random_image_layout():
+    """The random-code image used for large-model throughput runs has the
+    writer's layout: header, 64-byte aligned sections, no overlaps, norms 1."""
+    import numpy as np
+
+    img = fmt.RandomImage(dict(fmt.TINY_ARGS), seed=3)
+    head = fmt.HEADER.unpack(img.blob[: fmt.HEADER.size])
+    assert head == (fmt.MAGIC, fmt.VERSION, len(img.tensors), 6, 1)
+    spans = []
+    for e in img.tensors.values():
+        assert e["data_offset"] % fmt.ALIGNMENT == 0
+        spans.append((e["data_offset"], e["data_offset"] + e["data_bytes"]))
+        if "scale_offset" in e:
+            assert e["scale_offset"] % fmt.ALIGNMENT == 0
+            spans.append((e["scale_offset"], e["scale_offset"] + e["scale_bytes"]))
+            rows, cols = e["shape"]
+            assert e["data_bytes"] == rows * cols * 3 // 4
+            sc = np.frombuffer(img.blob[e["scale_offset"]: e["scale_offset"] + e["scale_bytes"]], dtype="<f4")
+            assert (sc > 0).all() and np.isfinite(sc).all()
+        else:
+            v = np.frombuffer(img.blob[e["data_offset"]: e["data_offset"] + e["data_bytes"]], dtype="<f4")
+            assert (v == 1.0).all()
+    spans.sort()
+    assert spans[0][0] >= fmt.HEADER.size
+    assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+    assert spans[-1][1] == len(img.blob)

@@ -219,14 +219,18 @@ def test_shipped_artifact_request(shipped_files_env, golden_shipped):
     assert res.generated[0] == g["generated"]
 
 
-def test_gqa_attention_op(tiny):
-    """The public attention op against torch's softmax attention."""
-    torch.manual_seed(3)
-    n, L, KV, rep, hd = 5, 40, 4, 2, 16
+@pytest.mark.parametrize("n,L,KV,rep,hd", [(5, 40, 4, 2, 16), (3, 300, 4, 8, 64), (2, 70, 2, 2, 128), (1, 256, 4, 8, 64)])
+def test_gqa_attention_op(tiny, n, L, KV, rep, hd):
+    """The public attention op against torch's softmax attention (head dims
+    16 / 32 take the warp-per-sequence kernel, 64 / 128 the per-head kernel;
+    300 positions exceed one pass of its 256 threads)."""
+    torch.manual_seed(3 + hd)
     q = torch.randn(n, KV * rep, hd)
     kk = torch.randn(n, L, KV, hd)
     vv = torch.randn(n, L, KV, hd)
-    lens = torch.tensor([1, 7, 40, 33, 12], dtype=torch.int32)
+    lens = torch.tensor([1, 7, 40, 33, 12, L, L - 1][:n], dtype=torch.int32).clamp(max=L)
+    if n <= 3:
+        lens[-1] = L
     out = ops.gqa_attention(q.cuda(), kk.cuda(), vv.cuda(), lens.cuda(), rep).cpu()
     for i in range(n):
         T = int(lens[i])

@@ -272,6 +272,116 @@ __global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb,
   }
 }
 
+// Decode attention, one CTA per (sequence, query head), for head dims the
+// warp-per-sequence kernel does not cover (64, 128) and few sequences (B=1
+// decode of large models): every thread scores its own positions (all K rows
+// in flight at once), the CTA reduces max and sum, then threads regroup as
+// (4-dim column, position stride) to accumulate probability * V, merged in a
+// fixed order.  Softmax as torch: exp(s - max), divide by the sum, then the
+// weighted sum of V rows (torch_benchmark.py:114-119).
+template <int HD>
+__global__ void __launch_bounds__(256) attn_head_kernel(
+    const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+    int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
+    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int H, int KV, int S, float denom) {
+  constexpr int CQ = HD / 4;        // float4 columns of a row
+  constexpr int G = 256 / CQ;       // position groups in the V pass
+  extern __shared__ __align__(16) float sa[];
+  float* sq = sa;                   // [HD]
+  float* red = sq + HD;             // [16]
+  float4* part = reinterpret_cast<float4*>(red + 16);  // [G][CQ]
+  float* sp = reinterpret_cast<float*>(part + G * CQ);  // [S] scores, then exp
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.x, h = blockIdx.y;
+  float* o = out + (int64_t)b * ldo + h * HD;
+  int T = len[b] + len_add;
+  T = T > S ? S : T;
+  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
+    if (tid < HD) o[tid] = 0.0f;
+    return;
+  }
+  const int kvr = KV * HD;
+  const int g = h / (H / KV);
+  const float4* kb = reinterpret_cast<const float4*>(kc + b * cstride + layer_off + g * HD);
+  const float4* vb = reinterpret_cast<const float4*>(vc + b * cstride + layer_off + g * HD);
+  if (tid < HD) sq[tid] = qb[(int64_t)b * ldq + h * HD + tid];
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int t = tid; t < T; t += 256) {
+    const float4* kr = kb + (int64_t)t * (kvr / 4);
+    float d = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CQ; ++j) {
+      const float4 k4 = __ldg(kr + j);
+      d = fmaf(sq[4 * j], k4.x, d);
+      d = fmaf(sq[4 * j + 1], k4.y, d);
+      d = fmaf(sq[4 * j + 2], k4.z, d);
+      d = fmaf(sq[4 * j + 3], k4.w, d);
+    }
+    d = __fdiv_rn(d, denom);
+    sp[t] = d;
+    mx = fmaxf(mx, d);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  float sum = 0.0f;
+  for (int t = tid; t < T; t += 256) {
+    const float e = expf(sp[t] - mx);
+    sp[t] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[8 + warp] = sum;
+  __syncthreads();
+  sum = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) sum += red[8 + w];
+  const int cq = tid % CQ, grp = tid / CQ;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = grp; t < T; t += G) {
+    const float wt = __fdiv_rn(sp[t], sum);
+    const float4 v4 = __ldg(vb + (int64_t)t * (kvr / 4) + cq);
+    acc.x = fmaf(wt, v4.x, acc.x);
+    acc.y = fmaf(wt, v4.y, acc.y);
+    acc.z = fmaf(wt, v4.z, acc.z);
+    acc.w = fmaf(wt, v4.w, acc.w);
+  }
+  part[grp * CQ + cq] = acc;
+  __syncthreads();
+  if (tid < CQ) {
+    float4 r = part[tid];
+    for (int k = 1; k < G; ++k) {
+      const float4 p = part[k * CQ + tid];
+      r.x += p.x; r.y += p.y; r.z += p.z; r.w += p.w;
+    }
+    reinterpret_cast<float4*>(o)[tid] = r;
+  }
+}
+
+// Shared memory of attn_head_kernel for S positions.
+static size_t attn_head_smem(int hd, int S) { return (size_t)(hd + 16) * 4 + 256 * 16 + (size_t)S * 4; }
+
+static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, const float* qb, int ldq,
+                             const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
+                             const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo, int S,
+                             float denom) {
+  const size_t smem = attn_head_smem(hd, S);
+  if (smem > 48 * 1024 || H > 65535 || (hd != 64 && hd != 128)) return false;
+  const dim3 grid(n, H);
+  if (hd == 64)
+    attn_head_kernel<64><<<grid, 256, smem, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add, flags, out,
+                                                  ldo, H, KV, S, denom);
+  else
+    attn_head_kernel<128><<<grid, 256, smem, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add, flags, out,
+                                                   ldo, H, KV, S, denom);
+  return true;
+}
+
 // Decode attention, one warp per sequence: the warp streams the sequence's
 // K and V rows 0..T-1 once (32/R rows per pass, R = KV*HD/16 lanes per row,
 // 16 dims per lane), prefetching the next pass's rows while it computes the
@@ -540,6 +650,9 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
     if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
                          layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom)) {
       Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
+                                w.pos, 1, w.flags, w.att, dim, S, M->denom)) {
+      Q6W_LAUNCH_CHECK("attn_head_kernel");
     } else {
     switch (M->hd) {
 #define Q6W_ATTN(HDV)                                                                          \
@@ -1210,6 +1323,11 @@ extern "C" int32_t q6w_gqa_attention(const float* queries, const float* keys, co
   if (launch_attn_rows(head_dim, kv_heads, groups_per_kv, grid, s, queries, ld, keys, values, kv_seq_stride, 0,
                        lengths, 0, nullptr, output, ld, max_len, denom)) {
     Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    return Q6W_OK;
+  }
+  if (launch_attn_head(head_dim, n, H, kv_heads, s, queries, ld, keys, values, kv_seq_stride, 0, lengths, 0, nullptr,
+                       output, ld, max_len, denom)) {
+    Q6W_LAUNCH_CHECK("attn_head_kernel");
     return Q6W_OK;
   }
   switch (head_dim) {

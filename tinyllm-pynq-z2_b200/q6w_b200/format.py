@@ -348,3 +348,53 @@ def write_synthetic(model_args, seed, output_path, manifest_path, std=0.02, over
     prov = {"synthetic": {"seed": int(seed), "init": f"normal(0, {std}) per quantized tensor, "
                           "torch.Generator(cpu).manual_seed(seed), drawn in file order; norms = 1.0"}}
     return write_q6w(state, model_args, output_path, manifest_path, prov, overwrite=overwrite)
+
+
+class RandomImage:
+    """An in-memory Q6W image with uniformly random 6-bit codes (every byte
+    pattern is a valid code stream) for throughput runs of models too large to
+    quantize on the host quickly.
+
+    Same layout as ``write_q6w`` (header, then per quantized tensor its scales
+    and packed rows, then the norms, every section 64-byte aligned) and the
+    attributes ``Q6WImage`` exposes (``blob``, ``tensors``, ``model_args``,
+    ``manifest``).  Row scales are ``1 / (18 * sqrt(cols))`` times U(0.5, 1.5),
+    so a matrix roughly preserves the magnitude of a normalised input; norms
+    are 1.  Values differ from any trained model, costs do not.
+    """
+
+    def __init__(self, model_args, seed=0):
+        self.model_args = dict(model_args)
+        n_layers = int(self.model_args["n_layers"])
+        shapes = _model_shapes(self.model_args)
+        qkeys, nkeys = quant_keys(n_layers), norm_keys(n_layers)
+        entries, off = [], HEADER.size
+        for key in qkeys:
+            rows, cols = shapes[key]
+            s_off = align_up(off)
+            d_off = align_up(s_off + 4 * rows)
+            off = d_off + rows * cols * 3 // 4
+            entries.append({"name": key, "shape": [rows, cols], "dtype": "signed_int6_twos_complement",
+                            "scale_offset": s_off, "scale_bytes": 4 * rows, "data_offset": d_off,
+                            "data_bytes": rows * cols * 3 // 4})
+        for key in nkeys:
+            d_off = align_up(off)
+            off = d_off + 4 * shapes[key][0]
+            entries.append({"name": key, "shape": list(shapes[key]), "dtype": "little_endian_float32",
+                            "data_offset": d_off, "data_bytes": 4 * shapes[key][0]})
+        rng = np.random.default_rng(int(seed))
+        blob = np.zeros(off, dtype=np.uint8)
+        blob[: HEADER.size] = np.frombuffer(HEADER.pack(MAGIC, VERSION, len(entries), 6, 1), dtype=np.uint8)
+        for e in entries:
+            lo, hi = e["data_offset"], e["data_offset"] + e["data_bytes"]
+            if e["dtype"] == "signed_int6_twos_complement":
+                rows, cols = e["shape"]
+                blob[lo:hi] = rng.integers(0, 256, hi - lo, dtype=np.uint8)
+                sc = (rng.uniform(0.5, 1.5, rows) / (18.0 * np.sqrt(cols))).astype("<f4")
+                blob[e["scale_offset"]: e["scale_offset"] + 4 * rows] = np.frombuffer(sc.tobytes(), dtype=np.uint8)
+            else:
+                blob[lo:hi] = np.frombuffer(np.ones(e["shape"][0], dtype="<f4").tobytes(), dtype=np.uint8)
+        self.blob = blob.tobytes()
+        self.tensors = {e["name"]: e for e in entries}
+        self.manifest = {"format": FORMAT_NAME, "model_args": self.model_args, "tensor_count": len(entries),
+                         "tensors": entries, "synthetic": {"seed": int(seed), "codes": "uniform random bytes"}}

@@ -249,6 +249,9 @@ class Q6WCudaTransformer:
         ga.k_cache, ga.v_cache = k.data_ptr(), v.data_ptr()
         ga.cache_seq_stride = k[0].numel()
         ga.step_logits = step_logits.data_ptr() if step_logits is not None else None
+        if prefill_event is not None and not prefill_event.cuda_event:
+            with torch.cuda.device(dev):
+                prefill_event.record()  # torch creates the CUDA event on its first record
         ga.prefill_event = prefill_event.cuda_event if prefill_event is not None else None
         with torch.cuda.device(dev):
             _lib.check(self._lib.q6w_generate_greedy(self._handle, ga, ws.data_ptr(), nbytes, _lib.stream_handle()),
