@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--only-main", action="store_true", help="skip the B=1, GEMV and CPU side measurements")
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
+    ap.add_argument("--profile-scaled-step", action="store_true",
+                    help="only run a short B=1 request (2 + 3 tokens) of the 1.1B-shape config and exit")
     return ap.parse_args()
 
 
@@ -489,6 +491,24 @@ def scaled_b1(dev, stream, reps=3):
             "peak_kind": f"{kind} hbm_gbs"}
 
 
+def profile_scaled_step():
+    """A short B=1 request of the 1.1B-shape config (2-token prompt, 3 tokens):
+    the launch list of its model steps is the profile of a scaled decode step."""
+    import torch
+
+    from q6w_b200 import format as fmt
+    from q6w_b200.model import Q6WCudaTransformer
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    model = Q6WCudaTransformer(fmt.RandomImage(dict(fmt.SCALED_ARGS), seed=7), device=dev)
+    pr = torch.tensor([[17, 2500]], dtype=torch.int32, device=dev)
+    ln = torch.tensor([2], dtype=torch.int32, device=dev)
+    sampled, n_sampled, *_ = model.generate_greedy_device(pr, ln, 2, 3)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_scaled_step": True, "sampled": sampled[0, : int(n_sampled[0])].tolist()}), flush=True)
+
+
 def profile_gemv(shape):
     """One B=1 GEMV shape, 4 launches on random data: the small case the
     ncu summaries under profiles/ are taken on."""
@@ -555,6 +575,8 @@ def main():
     a = parse()
     if a.profile_gemv:
         profile_gemv(a.profile_gemv)
+    elif a.profile_scaled_step:
+        profile_scaled_step()
     elif a.impl == "reference":
         run_reference(a)
     else:
