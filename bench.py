@@ -302,6 +302,7 @@ def run_b200(a):
     b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if rank == 0 and not a.only_main else None
     gemv = scaled_gemv(dev, stream) if rank == 0 and not a.only_main else None
     sb1 = scaled_b1(dev, stream) if rank == 0 and not a.only_main else None
+    pf = prefill_c3(model, rank, world, stream) if rank == 0 and not a.only_main else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -321,7 +322,7 @@ def run_b200(a):
                     "d2h_bytes_per_step": int(n * T * 4)},
             "gpu_launches": launches_per_gen * a.steps,
             "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len,
-            "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1,
+            "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1, "prefill": pf,
         }
         if not a.no_cpu_baseline and not a.only_main and world == 1:
             cores = cpu_cores()
@@ -445,6 +446,44 @@ def scaled_gemv(dev, stream, reps=10):
             "vocab_32000x2048": {"us_per_launch": round(vsec * 1e6, 2), "bytes": vbytes,
                                  "achieved_gbs": round(vbytes / vsec / 1e9, 1),
                                  "frac": round(vbytes / vsec / 1e9 / peak, 4)}}
+
+
+def prefill_c3(model, rank, world, stream, reps=3):
+    """Batched ragged prefill of the tiny model: 2048 prompts, lengths
+    U[8, 256], ids U[3, 4095] (one seed for all ranks), this rank's share
+    balanced by prompt tokens; last-position logits + filled KV caches in
+    one q6w_prefill call."""
+    import numpy as np
+    import torch
+
+    from q6w_b200 import dp
+
+    rng = np.random.default_rng(2048)
+    lens_all = rng.integers(8, 257, 2048)
+    ids_all = rng.integers(3, 4096, (2048, 256)).astype(np.int32)
+    mine = dp.balance_by_tokens(lens_all.tolist(), world)[rank]
+    lens = lens_all[mine].astype(np.int32)
+    L = int(lens.max())
+    pr = torch.from_numpy(np.ascontiguousarray(ids_all[mine, :L])).to(model.device)
+    ln = torch.from_numpy(lens).to(model.device)
+    total = int(lens.sum())
+    caches = model.new_batch_cache(len(mine))
+    for _ in range(2):
+        _, _, _, ws = model.prefill_batch_device(pr, ln, L, total, caches=caches)
+    model.check_device_status(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        model.prefill_batch_device(pr, ln, L, total, caches=caches)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    del caches
+    torch.cuda.empty_cache()
+    return {"workload": f"batched ragged prefill, tiny model: {len(mine)} of 2048 prompts, lengths U[8,256]",
+            "prompts": len(mine), "tokens": total, "ms": round(sec * 1e3, 3),
+            "prefill_tok_s": round(total / sec, 1), "prompts_s": round(len(mine) / sec, 1)}
 
 
 def scaled_b1(dev, stream, reps=3):

@@ -181,6 +181,29 @@ Q6W_API int32_t q6w_forward_batch(const q6w_model* model, int32_t n_seqs, const 
                           int64_t cache_seq_stride, float* logits, int32_t* argmax,
                           void* workspace, size_t workspace_bytes, q6w_stream_t stream);
 
+/* Workspace bytes of q6w_prefill for n_prompts prompts of total_tokens tokens
+ * together (0 if total_tokens is beyond the per-call limit of 2^22 rows). */
+Q6W_API size_t q6w_prefill_workspace_bytes(const q6w_model* model, int32_t n_prompts, int64_t total_tokens);
+
+/* Batched prefill of n_prompts independent prompts of ragged lengths:
+ * prompts [n_prompts, prompt_stride] and prompt_lens [n_prompts] are device
+ * arrays, 1 <= prompt_lens[i] <= max_prompt_len <= max_seq_len, and
+ * total_tokens is the sum of the lengths.  Fills every prompt's K/V cache rows
+ * 0..len-1 (prompt i at k_cache + i * cache_seq_stride) and writes the logits
+ * of each prompt's last position, [n_prompts, vocab] (or NULL), and their
+ * first-maximum argmax [n_prompts] (or NULL).  All prompt tokens run through
+ * the layers at once (rows are tokens; each token attends over its prompt's
+ * positions 0..j), so the result equals running CachedTransformer.step over
+ * every prompt position in order, the prompt loop of
+ * benchmarks/torch_benchmark.py:263-270.  Bad lengths, tokens or a total that
+ * does not match the lengths are flagged on the device (q6w_workspace_status)
+ * and the affected rows write nothing. */
+Q6W_API int32_t q6w_prefill(const q6w_model* model, int32_t n_prompts, const int32_t* prompts,
+                    const int32_t* prompt_lens, int32_t prompt_stride, int32_t max_prompt_len,
+                    int64_t total_tokens, float* k_cache, float* v_cache, int64_t cache_seq_stride,
+                    float* last_logits, int32_t* last_argmax, void* workspace, size_t workspace_bytes,
+                    q6w_stream_t stream);
+
 /* Greedy generation of n_seqs independent requests, entirely on the device:
  * token-by-token prefill of each (ragged) prompt, then greedy decode with
  * the reference's stop contract -- stop ids masked to -inf while fewer than

@@ -52,6 +52,7 @@ struct EpiArgs {
   float* vc;
   int64_t cache_stride;
   int64_t layer_off;
+  const int32_t* seq;  // cache row of activation row m (null: row m); prefill rows are tokens
   const float* rope_cos;
   const float* rope_sin;
   int32_t hd, q_rows, kv_rows;
@@ -141,12 +142,13 @@ __device__ __forceinline__ unsigned long long epilogue(const EpiArgs& ep, int m,
       b = rb;
     }
     float* dst;
+    const int64_t crow = ep.seq ? ep.seq[m] : m;
     if (v < ep.q_rows) {
       dst = ep.qbuf + (int64_t)m * ep.ldq + v;
     } else if (v < ep.q_rows + ep.kv_rows) {
-      dst = ep.kc + m * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v - ep.q_rows);
+      dst = ep.kc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v - ep.q_rows);
     } else {
-      dst = ep.vc + m * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
+      dst = ep.vc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
             (v - ep.q_rows - ep.kv_rows);
     }
     dst[0] = a;

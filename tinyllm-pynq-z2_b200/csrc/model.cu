@@ -44,6 +44,7 @@ struct Work {
   uint8_t* xs_img;   // tensor-core path: activation images (see tc.cuh)
   uint8_t* att_img;
   uint8_t* hs_img;
+  const int32_t* seq;  // cache row of each activation row (prefill: rows are tokens); null: row i
 };
 
 struct GraphKey {
@@ -100,6 +101,7 @@ static size_t layout(const q6w_model* M, int N, char* base, Work* w) {
   } else {
     t.xs_img = t.att_img = t.hs_img = nullptr;
   }
+  t.seq = nullptr;
   if (w) *w = t;
   return (size_t)(p - base);
 }
@@ -178,7 +180,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb,
                                                    int64_t layer_off, const int32_t* __restrict__ len,
                                                    int len_add, const int32_t* __restrict__ flags,
                                                    float* __restrict__ out, int ldo, int H, int KV,
-                                                   int S, float denom) {
+                                                   int S, float denom, const int32_t* __restrict__ seq) {
   extern __shared__ float sc[];
   constexpr int P = 32 / G;
   constexpr int HD = 16 * G;
@@ -196,8 +198,9 @@ __global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb,
   }
   const int g = h / (H / KV);
   const int kvr = KV * HD;
-  const float* kb = kc + b * cstride + layer_off + g * HD + 16 * part;
-  const float* vb = vc + b * cstride + layer_off + g * HD + 16 * part;
+  const int64_t crow = seq ? seq[b] : b;
+  const float* kb = kc + crow * cstride + layer_off + g * HD + 16 * part;
+  const float* vb = vc + crow * cstride + layer_off + g * HD + 16 * part;
   float q[16];
   {
     const float4* qp = reinterpret_cast<const float4*>(qb + (int64_t)b * ldq + h * HD + 16 * part);
@@ -283,7 +286,8 @@ template <int HD>
 __global__ void __launch_bounds__(256) attn_head_kernel(
     const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
-    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int H, int KV, int S, float denom) {
+    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int H, int KV, int S, float denom,
+    const int32_t* __restrict__ seq) {
   constexpr int CQ = HD / 4;        // float4 columns of a row
   constexpr int G = 256 / CQ;       // position groups in the V pass
   extern __shared__ __align__(16) float sa[];
@@ -302,8 +306,9 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
   }
   const int kvr = KV * HD;
   const int g = h / (H / KV);
-  const float4* kb = reinterpret_cast<const float4*>(kc + b * cstride + layer_off + g * HD);
-  const float4* vb = reinterpret_cast<const float4*>(vc + b * cstride + layer_off + g * HD);
+  const int64_t crow = seq ? seq[b] : b;
+  const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + g * HD);
+  const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + g * HD);
   if (tid < HD) sq[tid] = qb[(int64_t)b * ldq + h * HD + tid];
   __syncthreads();
   float mx = -INFINITY;
@@ -369,16 +374,16 @@ static size_t attn_head_smem(int hd, int S) { return (size_t)(hd + 16) * 4 + 256
 static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, const float* qb, int ldq,
                              const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo, int S,
-                             float denom) {
+                             float denom, const int32_t* seq = nullptr) {
   const size_t smem = attn_head_smem(hd, S);
   if (smem > 48 * 1024 || H > 65535 || (hd != 64 && hd != 128)) return false;
   const dim3 grid(n, H);
   if (hd == 64)
     attn_head_kernel<64><<<grid, 256, smem, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add, flags, out,
-                                                  ldo, H, KV, S, denom);
+                                                  ldo, H, KV, S, denom, seq);
   else
     attn_head_kernel<128><<<grid, 256, smem, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add, flags, out,
-                                                   ldo, H, KV, S, denom);
+                                                   ldo, H, KV, S, denom, seq);
   return true;
 }
 
@@ -392,7 +397,7 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
     const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
     const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom, int n,
-    uint8_t* __restrict__ out_img) {
+    uint8_t* __restrict__ out_img, const int32_t* __restrict__ seq) {
   constexpr int C = HD / 16;
   constexpr int R = KV * C;
   constexpr int PPW = 32 / R;
@@ -431,8 +436,9 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[j][i] = 0.0f;
   }
-  const float4* kb = reinterpret_cast<const float4*>(kc + b * cstride + layer_off + r * 16);
-  const float4* vb = reinterpret_cast<const float4*>(vc + b * cstride + layer_off + r * 16);
+  const int64_t crow = seq ? seq[b] : b;
+  const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + r * 16);
+  const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + r * 16);
   const int t_lane = lane / R;
   float4 kn[4], vn[4];
   {
@@ -526,18 +532,18 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
 static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st, const float* qb, int ldq,
                              const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo,
-                             int S, float denom, uint8_t* out_img = nullptr) {
+                             int S, float denom, uint8_t* out_img = nullptr, const int32_t* seq = nullptr) {
 #define Q6W_ROWS(HDV, KVV, REPV)                                                                          \
   if (hd == HDV && KV == KVV && rep == REPV) {                                                            \
     const int nb = ((int)grid.x + 3) / 4;                                                                 \
     if (out_img)                                                                                          \
       attn_warp_kernel<HDV, KVV, REPV, true><<<nb, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,      \
                                                                  len, len_add, flags, out, ldo, S,        \
-                                                                 denom, (int)grid.x, out_img);            \
+                                                                 denom, (int)grid.x, out_img, seq);       \
     else                                                                                                  \
       attn_warp_kernel<HDV, KVV, REPV, false><<<nb, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,     \
                                                                   len, len_add, flags, out, ldo, S,       \
-                                                                  denom, (int)grid.x, nullptr);           \
+                                                                  denom, (int)grid.x, nullptr, seq);      \
     return true;                                                                                          \
   }
   Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)
@@ -606,12 +612,14 @@ __global__ void keys_to_argmax_kernel(int n, unsigned long long* keys, int32_t* 
 // ---- step enqueue --------------------------------------------------------------
 
 static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
-                               const EpiArgs& vocab_ep, cudaStream_t st);
+                               const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab);
 static int tc_min_seqs();
 
+// One model step for n activation rows: embedding, the layers, and (unless
+// with_vocab is false) the vocab projection + argmax of every row.
 static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc, float* vc,
-                            int64_t cstride, const EpiArgs& vocab_ep, cudaStream_t st) {
-  if (M->use_tc && n >= tc_min_seqs()) return enqueue_step_tc(M, n, w, kc, vc, cstride, vocab_ep, st);
+                            int64_t cstride, const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab = true) {
+  if (M->use_tc && n >= tc_min_seqs()) return enqueue_step_tc(M, n, w, kc, vc, cstride, vocab_ep, st, with_vocab);
   const q6w_model_desc& d = M->d;
   const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
   embed_kernel<<<n < 2048 ? n : 2048, 128, 0, st>>>(d.tok_embeddings.packed,
@@ -622,6 +630,7 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
   memset(&ep, 0, sizeof(ep));
   ep.pos = w.pos;
   ep.flags = w.flags;
+  ep.seq = w.seq;
   const int warps = d.n_heads < 8 ? d.n_heads : 8;
   const dim3 agrid(n, (d.n_heads + warps - 1) / warps);
   const size_t asmem = (size_t)warps * S * sizeof(float);
@@ -648,10 +657,10 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
       if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "qkv linear: %s", cudaGetErrorString(e));
     }
     if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
-                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom)) {
+                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq)) {
       Q6W_LAUNCH_CHECK("attn_rows_kernel");
     } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
-                                w.pos, 1, w.flags, w.att, dim, S, M->denom)) {
+                                w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq)) {
       Q6W_LAUNCH_CHECK("attn_head_kernel");
     } else {
     switch (M->hd) {
@@ -660,7 +669,7 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
     attn_kernel<HDV / 16><<<agrid, warps * 32, asmem, st>>>(w.qb, dim, kc, vc, cstride,        \
                                                             layer_off, w.pos, 1, w.flags, w.att, \
                                                             dim, d.n_heads, d.n_kv_heads, S,   \
-                                                            M->denom);                         \
+                                                            M->denom, w.seq);                  \
     break;
       Q6W_ATTN(16) Q6W_ATTN(32) Q6W_ATTN(64) Q6W_ATTN(128) Q6W_ATTN(256) Q6W_ATTN(512)
 #undef Q6W_ATTN
@@ -697,6 +706,7 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
       if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "w2 linear: %s", cudaGetErrorString(e));
     }
   }
+  if (!with_vocab) return Q6W_OK;
   MatSet mv = {d.tok_embeddings.packed, nullptr, nullptr, d.tok_embeddings.scales, nullptr, nullptr,
                d.vocab_size, d.vocab_size, dim, 0, d.vocab_size / 2};
   EpiArgs v = vocab_ep;
@@ -784,7 +794,7 @@ static int32_t tc_set_attrs() {
 // enqueue_step; RMSNorm moves from the linear prologues into the epilogues
 // that produce each linear's input).
 static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
-                               const EpiArgs& vocab_ep, cudaStream_t st) {
+                               const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab) {
   const q6w_model_desc& d = M->d;
   const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
   embed_tc_kernel<<<(n * 16 + 127) / 128, 128, 0, st>>>(d.tok_embeddings.packed, d.tok_embeddings.scales,
@@ -798,6 +808,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
   base.eps = d.norm_eps;
   base.ep.pos = w.pos;
   base.ep.flags = w.flags;
+  base.ep.seq = w.seq;
   int32_t rc;
   for (int l = 0; l < d.n_layers; ++l) {
     const q6w_layer_weights& L = M->layers[l];
@@ -818,7 +829,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       if ((rc = tc_launch(tc::TEPI_QKV, a, M->sm_count, st))) return rc;
     }
     if (!launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, dim3(n), st, w.qb, dim, kc, vc,
-                          cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img))
+                          cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img, w.seq))
       return fail(Q6W_ERR_ARG, "no attention kernel for this head layout");
     Q6W_LAUNCH_CHECK("attn_rows_kernel");
     {
@@ -856,6 +867,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st))) return rc;
     }
   }
+  if (!with_vocab) return Q6W_OK;
   tc::TcArgs a = base;
   a.a_img = w.xs_img;
   a.K = dim;
@@ -871,6 +883,103 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
   a.ep.plen = w.plen;
   a.ep.vocab = d.vocab_size;
   return tc_launch(tc::TEPI_VOCAB, a, M->sm_count, st);
+}
+
+// ---- batched prefill: rows are prompt tokens --------------------------------
+
+// Row offset of every prompt (exclusive prefix sum of the lengths) and the
+// total, by one CTA; a length outside [1, max_len] counts as 0 and is flagged.
+__global__ void prefill_scan_kernel(int n, const int32_t* __restrict__ lens, int max_len, int32_t* __restrict__ off,
+                                    int32_t* err) {
+  __shared__ int64_t carry;
+  __shared__ int32_t part[32];
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    int v = 0;
+    if (i < n) {
+      v = lens[i];
+      if (v < 1 || v > max_len) {
+        atomicOr(err, 1);
+        v = 0;
+      }
+    }
+    int x = v;  // inclusive warp scan
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) part[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int t = lane < (int)(blockDim.x >> 5) ? part[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      part[lane] = t;
+    }
+    __syncthreads();
+    const int64_t before = carry + (warp ? part[warp - 1] : 0) + x - v;
+    if (i < n) off[i] = (int32_t)(before > 0x7fffffff ? 0x7fffffff : before);
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = before + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) off[n] = (int32_t)(carry > 0x7fffffff ? 0x7fffffff : carry);
+}
+
+// Token rows: row off[i] + j is token j of prompt i (cache row i, position j).
+// The prompts cover rows [0, off[n]) exactly once; rows from off[n] on (a
+// total that does not match the lengths) stay invalid and write nothing.
+__global__ void prefill_rows_kernel(int n, int rows, const int32_t* __restrict__ prompts, int stride,
+                                    const int32_t* __restrict__ lens, int max_len, int vocab,
+                                    const int32_t* __restrict__ off, Work w, int32_t* seq) {
+  const int covered = off[n] < rows ? off[n] : rows;
+  if (off[n] != rows && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(w.err, 1);
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t r = covered + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += nthreads) {
+    w.flags[r] = SEQ_INVALID;
+    w.tok[r] = -1;  // the embedding step re-validates rows: an invalid token keeps this one out
+    w.pos[r] = 0;
+    seq[r] = 0;
+  }
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int L = lens[i];
+    if (L < 1 || L > max_len) continue;
+    const int o = off[i];
+    for (int j = threadIdx.x; j < L; j += blockDim.x) {
+      const int64_t r = (int64_t)o + j;
+      if (r >= rows) break;
+      const int t = prompts[(int64_t)i * stride + j];
+      const bool ok = t >= 0 && t < vocab;
+      w.tok[r] = t;  // an out-of-range token is flagged (and kept out) by the embedding step
+      w.pos[r] = j;
+      w.flags[r] = ok ? 0 : SEQ_INVALID;
+      seq[r] = i;
+    }
+  }
+}
+
+// Final residual row of every prompt's last token -> row i of dst, argmax key cleared.
+__global__ void prefill_gather_kernel(int n, int rows, int dim, const int32_t* __restrict__ lens,
+                                      const int32_t* __restrict__ off, const float* __restrict__ x,
+                                      float* __restrict__ dst, unsigned long long* keys) {
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    int64_t r = (int64_t)off[i] + lens[i] - 1;
+    if (r < 0 || r >= rows) r = 0;
+    for (int k = threadIdx.x; k < dim; k += blockDim.x) dst[(int64_t)i * dim + k] = x[r * dim + k];
+    if (threadIdx.x == 0) keys[i] = 0ull;
+  }
+}
+
+__global__ void prefill_argmax_kernel(int n, const unsigned long long* __restrict__ keys, int32_t* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = argmax_index(keys[i]);
 }
 
 // Shapes the tensor-core step handles: dim 128, [wq|wk|wv] one N tile of at
@@ -1167,6 +1276,94 @@ static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& 
   return Q6W_OK;
 }
 
+// Rows of one q6w_prefill call (the tiled GEMM's grid has a 65535 x 128 row limit).
+constexpr int64_t kMaxPrefillRows = 1 << 22;
+
+// Workspace of q6w_prefill: the step workspace for total_tokens rows, then the
+// row -> cache-row map and the prompt offsets.
+static size_t prefill_layout(const q6w_model* M, int32_t n_prompts, int64_t total, char* base, Work* w,
+                             int32_t** seq, int32_t** off) {
+  const size_t step = layout(M, (int)total, base, w);
+  char* p = base ? base + step : nullptr;
+  const size_t a = ((size_t)4 * total + 255) & ~(size_t)255;
+  const size_t b = ((size_t)4 * (n_prompts + 1) + 255) & ~(size_t)255;
+  if (base) {
+    *seq = reinterpret_cast<int32_t*>(p);
+    *off = reinterpret_cast<int32_t*>(p + a);
+  }
+  return step + a + b;
+}
+
+extern "C" size_t q6w_prefill_workspace_bytes(const q6w_model* M, int32_t n_prompts, int64_t total_tokens) {
+  if (!M || n_prompts < 0 || total_tokens < 0 || total_tokens > kMaxPrefillRows) return 0;
+  return prefill_layout(M, n_prompts, total_tokens, nullptr, nullptr, nullptr, nullptr);
+}
+
+extern "C" int32_t q6w_prefill(const q6w_model* M, int32_t n_prompts, const int32_t* prompts,
+                               const int32_t* prompt_lens, int32_t prompt_stride, int32_t max_prompt_len,
+                               int64_t total_tokens, float* k_cache, float* v_cache, int64_t cache_seq_stride,
+                               float* last_logits, int32_t* last_argmax, void* workspace, size_t workspace_bytes,
+                               q6w_stream_t stream) {
+  clear_error();
+  if (!M) return fail(Q6W_ERR_ARG, "null model");
+  if (n_prompts < 0 || total_tokens < 0) return fail(Q6W_ERR_ARG, "n_prompts and total_tokens must be >= 0");
+  if (n_prompts == 0) return Q6W_OK;
+  if (total_tokens < n_prompts || total_tokens > kMaxPrefillRows)
+    return fail(Q6W_ERR_ARG, "total_tokens %lld must be in [n_prompts, %lld]", (long long)total_tokens,
+                (long long)kMaxPrefillRows);
+  if (!prompts || !prompt_lens) return fail(Q6W_ERR_ARG, "null prompts / prompt_lens");
+  if (max_prompt_len < 1 || max_prompt_len > M->d.max_seq_len || prompt_stride < max_prompt_len)
+    return fail(Q6W_ERR_ARG, "need 1 <= max_prompt_len <= max_seq_len (%d) and prompt_stride >= max_prompt_len",
+                M->d.max_seq_len);
+  if (last_logits && !aligned(last_logits, 8)) return fail(Q6W_ERR_ALIGN, "last_logits must be 8-byte aligned");
+  if (!workspace) return fail(Q6W_ERR_ARG, "null workspace");
+  if (!aligned(workspace, 256)) return fail(Q6W_ERR_ALIGN, "workspace must be 256-byte aligned");
+  const size_t need = prefill_layout(M, n_prompts, total_tokens, nullptr, nullptr, nullptr, nullptr);
+  if (workspace_bytes < need)
+    return fail(Q6W_ERR_ARG, "workspace of %zu bytes too small (%zu needed)", workspace_bytes, need);
+  int32_t st;
+  if ((st = check_cache(M, k_cache, v_cache, cache_seq_stride, n_prompts))) return st;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != M->device) return fail(Q6W_ERR_ARG, "model was created on device %d, current is %d", M->device, dev);
+  Work w;
+  int32_t *seq, *off;
+  prefill_layout(M, n_prompts, total_tokens, (char*)workspace, &w, &seq, &off);
+  const int rows = (int)total_tokens;
+  cudaStream_t s = (cudaStream_t)stream;
+  prefill_scan_kernel<<<1, 1024, 0, s>>>(n_prompts, prompt_lens, max_prompt_len, off, w.err);
+  Q6W_LAUNCH_CHECK("prefill_scan_kernel");
+  const int pgrid = n_prompts < 4096 ? n_prompts : 4096;
+  prefill_rows_kernel<<<pgrid, 256, 0, s>>>(
+      n_prompts, rows, prompts, prompt_stride, prompt_lens, max_prompt_len, M->d.vocab_size, off, w, seq);
+  Q6W_LAUNCH_CHECK("prefill_rows_kernel");
+  w.seq = seq;
+  EpiArgs none;
+  memset(&none, 0, sizeof(none));
+  if ((st = enqueue_step(M, rows, w, k_cache, v_cache, cache_seq_stride, none, s, false))) return st;
+  // vocab of the last token of each prompt, on the gathered rows
+  const int dim = M->d.dim;
+  prefill_gather_kernel<<<n_prompts < 4096 ? n_prompts : 4096, 128, 0, s>>>(n_prompts, rows, dim, prompt_lens, off,
+                                                                          w.x, w.qb, w.keys);
+  Q6W_LAUNCH_CHECK("prefill_gather_kernel");
+  const q6w_model_desc& d = M->d;
+  MatSet mv = {d.tok_embeddings.packed, nullptr, nullptr, d.tok_embeddings.scales, nullptr, nullptr,
+               d.vocab_size, d.vocab_size, dim, 0, d.vocab_size / 2};
+  EpiArgs v;
+  memset(&v, 0, sizeof(v));
+  v.y = last_logits;
+  v.ldy = d.vocab_size;
+  v.keys = w.keys;
+  v.vocab = d.vocab_size;
+  cudaError_t e = LinearLauncher<true, EPI_VOCAB>::run(w.qb, dim, n_prompts, d.norm, d.norm_eps, mv, v, s);
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "prefill vocab linear: %s", cudaGetErrorString(e));
+  if (last_argmax) {
+    prefill_argmax_kernel<<<grid_for(n_prompts, 256), 256, 0, s>>>(n_prompts, w.keys, last_argmax);
+    Q6W_LAUNCH_CHECK("prefill_argmax_kernel");
+  }
+  return Q6W_OK;
+}
+
 extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, void* workspace,
                                        size_t workspace_bytes, q6w_stream_t stream) {
   clear_error();
@@ -1335,7 +1532,7 @@ extern "C" int32_t q6w_gqa_attention(const float* queries, const float* keys, co
   case HDV:                                                                                          \
     attn_kernel<HDV / 16><<<grid, warps * 32, smem, s>>>(queries, ld, keys, values, kv_seq_stride, 0, \
                                                          lengths, 0, nullptr, output, ld, H,         \
-                                                         kv_heads, max_len, denom);                  \
+                                                         kv_heads, max_len, denom, nullptr);         \
     break;
     Q6W_ATTN2(16) Q6W_ATTN2(32) Q6W_ATTN2(64) Q6W_ATTN2(128) Q6W_ATTN2(256) Q6W_ATTN2(512)
 #undef Q6W_ATTN2

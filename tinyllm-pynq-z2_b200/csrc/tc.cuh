@@ -440,12 +440,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
           }
         }
         float* dst;
+        const int64_t crow = ep.seq ? ep.seq[m] : m;
         if (v0 < ep.q_rows)
           dst = ep.qbuf + m * ep.ldq + v0;
         else if (v0 < ep.q_rows + ep.kv_rows)
-          dst = ep.kc + m * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v0 - ep.q_rows);
+          dst = ep.kc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v0 - ep.q_rows);
         else
-          dst = ep.vc + m * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
+          dst = ep.vc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
                 (v0 - ep.q_rows - ep.kv_rows);
         float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll

@@ -25,7 +25,8 @@ EXPORTS = (
     "q6w_last_error", "q6w_abi_version", "q6w_unpack", "q6w_dequant", "q6w_linear",
     "q6w_model_create", "q6w_model_destroy", "q6w_workspace_bytes", "q6w_step",
     "q6w_forward_batch", "q6w_generate_greedy", "q6w_workspace_status", "q6w_linear_argmax",
-    "q6w_rmsnorm", "q6w_gqa_attention", "q6w_linear_argmax_noalloc",
+    "q6w_rmsnorm", "q6w_gqa_attention", "q6w_linear_argmax_noalloc", "q6w_prefill_workspace_bytes",
+    "q6w_prefill",
 )
 
 
@@ -91,6 +92,9 @@ def _declare(lib):
         "q6w_linear_argmax_noalloc": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                                 c_int64, c_int64, S]),
         "q6w_rmsnorm": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, S]),
+        "q6w_prefill_workspace_bytes": (c_size_t, [c_void_p, c_int32, c_int64]),
+        "q6w_prefill": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p,
+                                  c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_size_t, S]),
         "q6w_gqa_attention": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                         c_int32, c_int32, c_int32, c_int64, S]),
     }

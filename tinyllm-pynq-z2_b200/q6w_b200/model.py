@@ -217,6 +217,68 @@ class Q6WCudaTransformer:
                 ws.data_ptr(), nbytes, _lib.stream_handle()), "q6w_forward_batch")
         return lg, am
 
+    def _prefill_workspace(self, n_prompts, total_tokens):
+        need = int(self._lib.q6w_prefill_workspace_bytes(self._handle, int(n_prompts), int(total_tokens)))
+        if need == 0:
+            raise ValueError(f"{total_tokens} prompt tokens exceed the per-call prefill limit")
+        buf = getattr(self, "_pws", None)
+        if buf is None or buf.numel() < need:
+            raw = torch.zeros(need + 256, dtype=torch.uint8, device=self.device)
+            off = (-raw.data_ptr()) % 256
+            buf = raw[off: off + need]
+            self._pws = buf
+        return buf, need
+
+    def prefill_batch_device(self, prompts, prompt_lens, max_prompt_len, total_tokens, caches=None, logits=True,
+                             argmax=True):
+        """Batched prefill on device arrays (no host sync inside).
+
+        ``prompts``: device int32 [n, stride]; ``prompt_lens``: device int32 [n];
+        ``total_tokens``: the sum of the lengths.  Returns (last_logits
+        [n, vocab] or None, last_argmax [n] or None, caches, workspace).
+        """
+        n = int(prompts.shape[0])
+        if caches is None:
+            caches = self.new_batch_cache(n)
+        k, v = caches
+        self._check_cache(k, v, n)
+        lg = torch.empty((n, self.args.vocab_size), dtype=torch.float32, device=self.device) if logits else None
+        am = torch.empty(n, dtype=torch.int32, device=self.device) if argmax else None
+        ws, nbytes = self._prefill_workspace(n, total_tokens)
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.q6w_prefill(
+                self._handle, n, prompts.data_ptr(), prompt_lens.data_ptr(), int(prompts.shape[1]),
+                int(max_prompt_len), int(total_tokens), k.data_ptr(), v.data_ptr(), k[0].numel(),
+                lg.data_ptr() if lg is not None else None, am.data_ptr() if am is not None else None,
+                ws.data_ptr(), nbytes, _lib.stream_handle()), "q6w_prefill")
+        return lg, am, caches, ws
+
+    def prefill_batch(self, prompts):
+        """Prefill a list of prompt id lists at once: (last_logits [B, vocab],
+        (K, V) caches [B, n_layers, max_seq_len, n_kv_heads, head_dim]).
+
+        The logits of prompt i equal those ``step`` returns at its last
+        position after stepping through the prompt in order
+        (torch_benchmark.py:263-264), and cache slice i equals that run's cache.
+        """
+        n = len(prompts)
+        lens = [len(p) for p in prompts]
+        if n == 0:
+            raise ValueError("no prompts")
+        if min(lens) < 1:
+            raise ValueError("every prompt needs at least one token")
+        if max(lens) > self.args.max_seq_len:
+            raise ValueError("Prompt exceeds the model context")
+        L = max(lens)
+        host = np.zeros((n, L), dtype=np.int32)
+        for i, p in enumerate(prompts):
+            host[i, : len(p)] = p
+        pr = torch.from_numpy(host).to(self.device)
+        ln = torch.tensor(lens, dtype=torch.int32, device=self.device)
+        lg, _, caches, ws = self.prefill_batch_device(pr, ln, L, sum(lens), argmax=False)
+        self.check_device_status(ws)
+        return lg, caches
+
     def generate_greedy_device(self, prompts, prompt_lens, max_prompt_len, new_tokens, stop_ids=(),
                                min_new_tokens=0, caches=None, keep_logits=False, prefill_event=None):
         """Device-resident greedy generation (no host sync inside).
