@@ -299,10 +299,13 @@ def run_b200(a):
 
     # ---- dominant kernel alone: decode attention over this run's caches
     roof = attention_roofline(model, caches, n, P + T - 1, stream)
-    b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if rank == 0 and not a.only_main else None
-    gemv = scaled_gemv(dev, stream) if rank == 0 and not a.only_main else None
-    sb1 = scaled_b1(dev, stream) if rank == 0 and not a.only_main else None
-    pf = prefill_c3(model, rank, world, stream) if rank == 0 and not a.only_main else None
+    # single-GPU side measurements (B=1 latency, GEMV, 1.1B-shape decode, prefill): N=1 runs only, so
+    # no rank waits on a collective while rank 0 measures
+    side = world == 1 and not a.only_main
+    b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if side else None
+    gemv = scaled_gemv(dev, stream) if side else None
+    sb1 = scaled_b1(dev, stream) if side else None
+    pf = prefill_c3(model, rank, world, stream) if side else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -519,6 +522,20 @@ def scaled_b1(dev, stream, reps=3):
     d, t = statistics.median(dec), statistics.median(tot)
     # decode steps: T - 1 model steps after the prefill part (P steps)
     step_s = d / (T - 1)
+    # B=64: 64 independent requests of the same shape in one batched loop
+    n64 = 64
+    pr64 = torch.randint(3, args["vocab_size"], (n64, P), generator=g, dtype=torch.int32).to(dev)
+    ln64 = torch.full((n64,), P, dtype=torch.int32, device=dev)
+    caches64 = model.new_batch_cache(n64)
+    model.generate_greedy_device(pr64, ln64, P, T, caches=caches64)
+    torch.cuda.synchronize()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    model.generate_greedy_device(pr64, ln64, P, T, caches=caches64, prefill_event=e1)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    d64, t64 = e1.elapsed_time(e2) / 1e3, e0.elapsed_time(e2) / 1e3
+    del caches64
     wbytes = sum(e["data_bytes"] + e.get("scale_bytes", 0) for e in model.image.tensors.values())
     peak, kind = measured_peaks()
     del model, caches
@@ -527,7 +544,9 @@ def scaled_b1(dev, stream, reps=3):
             "decode_tok_s": round((T - 1) / d, 1), "request_tok_s": round(T / t, 1),
             "us_per_model_step": round(step_s * 1e6, 2), "weight_bytes_per_step": wbytes,
             "weights_gbs": round(wbytes / step_s / 1e9, 1), "frac_of_hbm": round(wbytes / step_s / 1e9 / peak, 4),
-            "peak_kind": f"{kind} hbm_gbs"}
+            "peak_kind": f"{kind} hbm_gbs",
+            "b64": {"decode_tok_s": round(n64 * (T - 1) / d64, 1), "request_tok_s": round(n64 * T / t64, 1),
+                    "us_per_model_step": round(d64 / (T - 1) * 1e6, 2)}}
 
 
 def profile_scaled_step():
