@@ -50,8 +50,8 @@ def parse():
     ap.add_argument("--only-main", action="store_true", help="skip the B=1, GEMV and CPU side measurements")
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
-    ap.add_argument("--profile-scaled-step", action="store_true",
-                    help="only run a short B=1 request (2 + 3 tokens) of the 1.1B-shape config and exit")
+    ap.add_argument("--profile-scaled-step", type=int, nargs="?", const=1, default=None, metavar="N",
+                    help="only run N short requests (2 + 3 tokens, default N=1) of the 1.1B-shape config and exit")
     return ap.parse_args()
 
 
@@ -549,8 +549,8 @@ def scaled_b1(dev, stream, reps=3):
                     "us_per_model_step": round(d64 / (T - 1) * 1e6, 2)}}
 
 
-def profile_scaled_step():
-    """A short B=1 request of the 1.1B-shape config (2-token prompt, 3 tokens):
+def profile_scaled_step(n=1):
+    """n short requests of the 1.1B-shape config (2-token prompts, 3 tokens):
     the launch list of its model steps is the profile of a scaled decode step."""
     import torch
 
@@ -560,8 +560,8 @@ def profile_scaled_step():
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     model = Q6WCudaTransformer(fmt.RandomImage(dict(fmt.SCALED_ARGS), seed=7), device=dev)
-    pr = torch.tensor([[17, 2500]], dtype=torch.int32, device=dev)
-    ln = torch.tensor([2], dtype=torch.int32, device=dev)
+    pr = torch.tensor([[17, 2500]] * n, dtype=torch.int32, device=dev)
+    ln = torch.full((n,), 2, dtype=torch.int32, device=dev)
     sampled, n_sampled, *_ = model.generate_greedy_device(pr, ln, 2, 3)
     torch.cuda.synchronize()
     print(json.dumps({"profile_scaled_step": True, "sampled": sampled[0, : int(n_sampled[0])].tolist()}), flush=True)
@@ -634,7 +634,7 @@ def main():
     if a.profile_gemv:
         profile_gemv(a.profile_gemv)
     elif a.profile_scaled_step:
-        profile_scaled_step()
+        profile_scaled_step(a.profile_scaled_step)
     elif a.impl == "reference":
         run_reference(a)
     else:

@@ -316,3 +316,36 @@ def test_b1_cluster_kernel_long_context(tmp_path_factory, monkeypatch):
     assert float((a.logits[0, :n] - b.logits[0, :n]).abs().max()) <= LOGIT_TOL
     summary = BatchScorer(orc).verify_greedy([p], [a.sampled[0]], new)
     assert summary["failures"] == []
+
+
+@pytest.mark.parametrize("n", [16, 64, 100])
+def test_general_tensor_core_step(tmp_path_factory, monkeypatch, n):
+    """The general tcgen05 linears (weights as the MMA's M operand, the three
+    bf16 activation parts stacked as N) on a 1.1B-shape layer: against the SIMT
+    step on the same inputs and the oracle on a sample."""
+    args = dict(fmt.SCALED_ARGS, n_layers=1, max_seq_len=16)
+    b, m = small_model_files(tmp_path_factory, args, 5, f"tcg{n}")
+    tc_model = Q6WCudaTransformer.from_q6w(b, m)
+    monkeypatch.setenv("Q6W_DISABLE_TCG", "1")
+    simt_model = Q6WCudaTransformer.from_q6w(b, m)
+    orc = OracleModel.from_q6w(b, m)
+    g = torch.Generator().manual_seed(200 + n)
+    T = 4
+    toks = torch.randint(0, args["vocab_size"], (T, n), generator=g).int()
+    outs = []
+    for mdl in (tc_model, simt_model):
+        k, v = mdl.new_batch_cache(n)
+        for t in range(T):
+            lg, am = mdl.forward_batch(toks[t].cuda(), torch.full((n,), t, dtype=torch.int32).cuda(), k, v,
+                                       argmax=True)
+        outs.append((lg.cpu(), am.cpu(), k[:, :, :T].cpu(), v[:, :, :T].cpu()))
+    (a_lg, a_am, a_k, a_v), (b_lg, b_am, b_k, b_v) = outs
+    assert float((a_lg - b_lg).abs().max()) <= LOGIT_TOL
+    assert float((a_k - b_k).abs().max()) <= 1e-4 and float((a_v - b_v).abs().max()) <= 1e-4
+    assert torch.equal(a_am.long(), a_lg.argmax(1))
+    for i in range(0, n, max(1, n // 4)):
+        ko, vo = orc.new_cache()
+        with torch.inference_mode():
+            for t in range(T):
+                want = orc.step(int(toks[t, i]), t, ko, vo)
+        assert float((a_lg[i] - want).abs().max()) <= LOGIT_TOL, i

@@ -26,6 +26,9 @@
 #include "b1.cuh"
 #include "launch.cuh"
 #include "tc.cuh"
+#include "tcg.cuh"
+
+#include <cudaTypedefs.h>
 
 namespace q6w {
 
@@ -65,7 +68,8 @@ struct q6w_model {
   cudaGraphExec_t exec = nullptr;
   q6w::GraphKey key;
   bool have_key = false;
-  bool use_tc = false;  // shapes qualify for the tensor-core batched path
+  bool use_tc = false;  // shapes qualify for the tensor-core batched path (dim 128)
+  bool use_tcg = false; // shapes qualify for the general tensor-core linears (any width)
   int sm_count = 148;
   bool use_b1 = false;  // shapes qualify for the single-request cluster kernel
   size_t b1_smem = 0;
@@ -94,7 +98,7 @@ static size_t layout(const q6w_model* M, int N, char* base, Work* w) {
   t.plen = (int32_t*)carve(p, 4 * (size_t)N);
   t.gen = (int32_t*)carve(p, 4 * (size_t)N);
   t.flags = (int32_t*)carve(p, 4 * (size_t)N);
-  if (M->use_tc) {
+  if (M->use_tc || M->use_tcg) {
     t.xs_img = (uint8_t*)carve(p, tc::img_bytes(N, d.dim));
     t.att_img = (uint8_t*)carve(p, tc::img_bytes(N, d.dim));
     t.hs_img = (uint8_t*)carve(p, tc::img_bytes(N, d.hidden_dim));
@@ -614,12 +618,16 @@ __global__ void keys_to_argmax_kernel(int n, unsigned long long* keys, int32_t* 
 static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
                                const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab);
 static int tc_min_seqs();
+static int tcg_min_rows();
+static int32_t enqueue_step_tcg(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
+                                const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab);
 
 // One model step for n activation rows: embedding, the layers, and (unless
 // with_vocab is false) the vocab projection + argmax of every row.
 static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc, float* vc,
                             int64_t cstride, const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab = true) {
   if (M->use_tc && n >= tc_min_seqs()) return enqueue_step_tc(M, n, w, kc, vc, cstride, vocab_ep, st, with_vocab);
+  if (M->use_tcg && n >= tcg_min_rows()) return enqueue_step_tcg(M, n, w, kc, vc, cstride, vocab_ep, st, with_vocab);
   const q6w_model_desc& d = M->d;
   const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
   embed_kernel<<<n < 2048 ? n : 2048, 128, 0, st>>>(d.tok_embeddings.packed,
@@ -982,6 +990,199 @@ __global__ void prefill_argmax_kernel(int n, const unsigned long long* __restric
   if (i < n) out[i] = argmax_index(keys[i]);
 }
 
+// ---- general tensor-core step (tcg.cuh) -------------------------------------
+
+// Shapes the general tensor-core linears handle: K (dim, hidden) multiples of
+// 64; wq|wk|wv, wo, w2 and vocab rows in whole 128-row tiles; W1/W3 in
+// 64-pair tiles.
+static bool tcg_shapes_ok(const q6w_model_desc& d, int kvr) {
+  return d.dim % 128 == 0 && d.hidden_dim % 64 == 0 && kvr % 128 == 0 && d.vocab_size % 128 == 0 && d.dim >= 256;
+}
+
+static cudaError_t tcg_set_attrs() {
+  const int smem = (int)tcg::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_VOCAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return e;
+}
+
+// Activation rows from which the general tensor-core linears run (below: the
+// SIMT GEMV / GEMM).
+static int tcg_min_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q6W_TCG_MIN_ROWS");
+    v = e ? atoi(e) : 16;
+    if (v < 1) v = 1;
+  }
+  return v;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link to libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// 2-D uint8 tensor map over a packed matrix [rows][K*3/4], box 48 bytes x box_rows.
+static int32_t weight_map(CUtensorMap* map, const uint8_t* q, int rows, int K, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(Q6W_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (!aligned(q, 16)) return fail(Q6W_ERR_ALIGN, "weights must be 16-byte aligned for the tensor-core linears");
+  const cuuint64_t rb = (cuuint64_t)K * 3 / 4;
+  cuuint64_t gdim[2] = {rb, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {rb};
+  cuuint32_t box[2] = {48, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), gdim, gstride, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(Q6W_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q6W_OK;
+}
+
+static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st) {
+  const bool glu = epi == tcg::GEPI_GLU;
+  const int wtiles = glu ? a.ms.n_pairs / (tcg::kWR / 2) : 2 * a.ms.n_pairs / tcg::kWR;
+  const int items = wtiles * ((a.n + tcg::kAR - 1) / tcg::kAR);
+  const int grid = items < sms ? items : sms;
+  tcg::GMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  int32_t rc;
+  if (glu) {
+    if ((rc = weight_map(&maps.m[0], a.ms.q0, a.ms.n_pairs, a.ms.cols, tcg::kWR / 2))) return rc;
+    if ((rc = weight_map(&maps.m[1], a.ms.q1, a.ms.n_pairs, a.ms.cols, tcg::kWR / 2))) return rc;
+  } else {
+    const int total = 2 * a.ms.n_pairs;
+    if ((rc = weight_map(&maps.m[0], a.ms.q0, a.ms.end0, a.ms.cols, tcg::kWR))) return rc;
+    if (a.ms.end1 > a.ms.end0 && (rc = weight_map(&maps.m[1], a.ms.q1, a.ms.end1 - a.ms.end0, a.ms.cols, tcg::kWR)))
+      return rc;
+    if (total > a.ms.end1 && (rc = weight_map(&maps.m[2], a.ms.q2, total - a.ms.end1, a.ms.cols, tcg::kWR)))
+      return rc;
+  }
+  switch (epi) {
+    case tcg::GEPI_QKV: tcg::tcg_kernel<tcg::GEPI_QKV><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
+    case tcg::GEPI_RESID: tcg::tcg_kernel<tcg::GEPI_RESID><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
+    case tcg::GEPI_GLU: tcg::tcg_kernel<tcg::GEPI_GLU><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
+    default: tcg::tcg_kernel<tcg::GEPI_VOCAB><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
+  }
+  Q6W_LAUNCH_CHECK("tcg_kernel");
+  return Q6W_OK;
+}
+
+static int32_t tcg_image(const float* x, int ldx, int n, int K, const float* g, float eps, uint8_t* img,
+                         cudaStream_t st) {
+  tcg::image_kernel<<<(n + 3) / 4, 128, 0, st>>>(x, ldx, n, K, g, eps, img);
+  Q6W_LAUNCH_CHECK("image_kernel");
+  return Q6W_OK;
+}
+
+// The batched step with every linear on the general tensor-core kernel: the
+// inputs of the linears become activation images (RMSNorm fused where the
+// reference normalises), attention as in the SIMT step.
+static int32_t enqueue_step_tcg(const q6w_model* M, int n, const Work& w, float* kc, float* vc, int64_t cstride,
+                                const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab) {
+  const q6w_model_desc& d = M->d;
+  const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
+  embed_kernel<<<n < 2048 ? n : 2048, 128, 0, st>>>(d.tok_embeddings.packed, d.tok_embeddings.scales, dim,
+                                                    d.vocab_size, S, n, w);
+  Q6W_LAUNCH_CHECK("embed_kernel");
+  tcg::GArgs base;
+  memset(&base, 0, sizeof(base));
+  base.n = n;
+  base.err = w.err;
+  base.ep.pos = w.pos;
+  base.ep.flags = w.flags;
+  base.ep.seq = w.seq;
+  int32_t rc;
+  const int warps = d.n_heads < 8 ? d.n_heads : 8;
+  const dim3 agrid(n, (d.n_heads + warps - 1) / warps);
+  for (int l = 0; l < d.n_layers; ++l) {
+    const q6w_layer_weights& L = M->layers[l];
+    const int64_t layer_off = (int64_t)l * S * kvr;
+    if ((rc = tcg_image(w.x, dim, n, dim, L.attention_norm, d.norm_eps, w.xs_img, st))) return rc;
+    {
+      tcg::GArgs a = base;
+      a.img = w.xs_img;
+      a.K = dim;
+      a.ms = {L.wq.packed, L.wk.packed, L.wv.packed, L.wq.scales, L.wk.scales, L.wv.scales,
+              dim, dim + kvr, dim, 0, (dim + 2 * kvr) / 2};
+      a.ep.qbuf = w.qb; a.ep.ldq = dim;
+      a.ep.kc = kc; a.ep.vc = vc; a.ep.cache_stride = cstride; a.ep.layer_off = layer_off;
+      a.ep.rope_cos = d.rope_cos; a.ep.rope_sin = d.rope_sin;
+      a.ep.hd = M->hd; a.ep.q_rows = dim; a.ep.kv_rows = kvr;
+      if ((rc = tcg_launch(tcg::GEPI_QKV, a, M->sm_count, st))) return rc;
+    }
+    if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
+                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq)) {
+      Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
+                                w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq)) {
+      Q6W_LAUNCH_CHECK("attn_head_kernel");
+    } else {
+      return fail(Q6W_ERR_ARG, "no attention kernel for head_dim %d on the tensor-core step", M->hd);
+    }
+    if ((rc = tcg_image(w.att, dim, n, dim, nullptr, 0.f, w.att_img, st))) return rc;
+    {
+      tcg::GArgs a = base;
+      a.img = w.att_img;
+      a.K = dim;
+      a.ms = {L.wo.packed, nullptr, nullptr, L.wo.scales, nullptr, nullptr, dim, dim, dim, 0, dim / 2};
+      a.ep.y = w.x; a.ep.ldy = dim;
+      if ((rc = tcg_launch(tcg::GEPI_RESID, a, M->sm_count, st))) return rc;
+    }
+    if ((rc = tcg_image(w.x, dim, n, dim, L.ffn_norm, d.norm_eps, w.xs_img, st))) return rc;
+    {
+      tcg::GArgs a = base;
+      a.img = w.xs_img;
+      a.K = dim;
+      a.ms = {L.w1.packed, L.w3.packed, nullptr, L.w1.scales, L.w3.scales, nullptr, hid, hid, dim, 1, hid};
+      a.ep.y = w.hb; a.ep.ldy = hid;
+      if ((rc = tcg_launch(tcg::GEPI_GLU, a, M->sm_count, st))) return rc;
+    }
+    if ((rc = tcg_image(w.hb, hid, n, hid, nullptr, 0.f, w.hs_img, st))) return rc;
+    {
+      tcg::GArgs a = base;
+      a.img = w.hs_img;
+      a.K = hid;
+      a.ms = {L.w2.packed, nullptr, nullptr, L.w2.scales, nullptr, nullptr, dim, dim, hid, 0, dim / 2};
+      a.ep.y = w.x; a.ep.ldy = dim;
+      if ((rc = tcg_launch(tcg::GEPI_RESID, a, M->sm_count, st))) return rc;
+    }
+  }
+  if (!with_vocab) return Q6W_OK;
+  if ((rc = tcg_image(w.x, dim, n, dim, d.norm, d.norm_eps, w.xs_img, st))) return rc;
+  tcg::GArgs a = base;
+  a.img = w.xs_img;
+  a.K = dim;
+  a.ms = {d.tok_embeddings.packed, nullptr, nullptr, d.tok_embeddings.scales, nullptr, nullptr,
+          d.vocab_size, d.vocab_size, dim, 0, d.vocab_size / 2};
+  a.ep = vocab_ep;
+  a.ep.pos = w.pos;
+  a.ep.flags = w.flags;
+  a.ep.keys = w.keys;
+  a.ep.gen = w.gen;
+  a.ep.plen = w.plen;
+  a.ep.vocab = d.vocab_size;
+  return tcg_launch(tcg::GEPI_VOCAB, a, M->sm_count, st);
+}
+
 // Shapes the tensor-core step handles: dim 128, [wq|wk|wv] one N tile of at
 // most 256 rows in 32-row chunks, hidden a multiple of 128, vocab a multiple
 // of 256, and an instantiated streaming-attention layout.
@@ -1134,6 +1335,12 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
     if (M->use_tc && (st = tc_set_attrs())) {
       delete M;
       return st;
+    }
+    const char* offg = getenv("Q6W_DISABLE_TCG");
+    M->use_tcg = !M->use_tc && !(offg && offg[0] == '1') && major == 10 && tcg_shapes_ok(d, kvr);
+    if (M->use_tcg && tcg_set_attrs() != cudaSuccess) {
+      cudaGetLastError();
+      M->use_tcg = false;  // the SIMT kernels still serve every shape
     }
     const char* off1 = getenv("Q6W_DISABLE_B1");
     M->use_b1 = !(off1 && off1[0] == '1') && major == 10 && b1_shapes_ok(M, &M->b1_smem);
