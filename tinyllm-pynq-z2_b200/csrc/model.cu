@@ -996,7 +996,11 @@ __global__ void prefill_argmax_kernel(int n, const unsigned long long* __restric
 // 64; wq|wk|wv, wo, w2 and vocab rows in whole 128-row tiles; W1/W3 in
 // 64-pair tiles.
 static bool tcg_shapes_ok(const q6w_model_desc& d, int kvr) {
-  return d.dim % 128 == 0 && d.hidden_dim % 64 == 0 && kvr % 128 == 0 && d.vocab_size % 128 == 0 && d.dim >= 256;
+  if (d.dim > 8 * tcg::kImgThreads * tcg::kImgChunks || d.hidden_dim > 8 * tcg::kImgThreads * tcg::kImgChunks)
+    return false;
+  // K (dim, hidden) in whole packed groups of kG x 64 columns
+  return d.dim % (64 * tcg::kG) == 0 && d.hidden_dim % (64 * tcg::kG) == 0 && d.dim >= 256 && d.dim % 128 == 0 &&
+         kvr % 128 == 0 && d.vocab_size % 128 == 0;
 }
 
 static cudaError_t tcg_set_attrs() {
@@ -1040,7 +1044,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// 2-D uint8 tensor map over a packed matrix [rows][K*3/4], box 48 bytes x box_rows.
+// 2-D uint8 tensor map over a packed matrix [rows][K*3/4], box 48 kG bytes x box_rows.
 static int32_t weight_map(CUtensorMap* map, const uint8_t* q, int rows, int K, int box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return fail(Q6W_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -1048,7 +1052,7 @@ static int32_t weight_map(CUtensorMap* map, const uint8_t* q, int rows, int K, i
   const cuuint64_t rb = (cuuint64_t)K * 3 / 4;
   cuuint64_t gdim[2] = {rb, (cuuint64_t)rows};
   cuuint64_t gstride[1] = {rb};
-  cuuint32_t box[2] = {48, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {48 * tcg::kG, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), gdim, gstride, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1061,7 +1065,10 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
   const bool glu = epi == tcg::GEPI_GLU;
   const int wtiles = glu ? a.ms.n_pairs / (tcg::kWR / 2) : 2 * a.ms.n_pairs / tcg::kWR;
   const int items = wtiles * ((a.n + tcg::kAR - 1) / tcg::kAR);
-  const int grid = items < sms ? items : sms;
+  const int nks = a.K / 64;
+  // split K over a cluster while the tiles alone would leave SMs idle
+  int C = 1;
+  while (C < tcg::kMaxSplit && items * C * 2 <= sms && nks % (C * 2) == 0) C *= 2;
   tcg::GMaps maps;
   memset(&maps, 0, sizeof(maps));
   int32_t rc;
@@ -1076,19 +1083,33 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
     if (total > a.ms.end1 && (rc = weight_map(&maps.m[2], a.ms.q2, total - a.ms.end1, a.ms.cols, tcg::kWR)))
       return rc;
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(items * C));
+  cfg.blockDim = dim3(tcg::kThreads);
+  cfg.dynamicSmemBytes = tcg::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   switch (epi) {
-    case tcg::GEPI_QKV: tcg::tcg_kernel<tcg::GEPI_QKV><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
-    case tcg::GEPI_RESID: tcg::tcg_kernel<tcg::GEPI_RESID><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
-    case tcg::GEPI_GLU: tcg::tcg_kernel<tcg::GEPI_GLU><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
-    default: tcg::tcg_kernel<tcg::GEPI_VOCAB><<<grid, tcg::kThreads, tcg::kSmem, st>>>(a, maps); break;
+    case tcg::GEPI_QKV: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_QKV>, a, maps); break;
+    case tcg::GEPI_RESID: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_RESID>, a, maps); break;
+    case tcg::GEPI_GLU: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_GLU>, a, maps); break;
+    default: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_VOCAB>, a, maps); break;
   }
-  Q6W_LAUNCH_CHECK("tcg_kernel");
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tcg_kernel launch: %s", cudaGetErrorString(e));
   return Q6W_OK;
 }
 
 static int32_t tcg_image(const float* x, int ldx, int n, int K, const float* g, float eps, uint8_t* img,
                          cudaStream_t st) {
-  tcg::image_kernel<<<(n + 3) / 4, 128, 0, st>>>(x, ldx, n, K, g, eps, img);
+  if (K % 8 || K > 8 * tcg::kImgThreads * tcg::kImgChunks) return fail(Q6W_ERR_ARG, "image of K=%d unsupported", K);
+  tcg::image_kernel<<<n, tcg::kImgThreads, 0, st>>>(x, ldx, n, K, g, eps, img);
   Q6W_LAUNCH_CHECK("image_kernel");
   return Q6W_OK;
 }
