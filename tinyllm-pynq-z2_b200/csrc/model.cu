@@ -1003,6 +1003,10 @@ static bool tcg_shapes_ok(const q6w_model_desc& d, int kvr) {
          kvr % 128 == 0 && d.vocab_size % 128 == 0;
 }
 
+// Clusters of C CTAs (index log2 C) that can be resident at once: a cluster
+// sits inside one GPC, so fewer than sm_count / C clusters fit.
+static int g_tcg_clusters[4] = {0, 0, 0, 0};
+
 static cudaError_t tcg_set_attrs() {
   const int smem = (int)tcg::kSmem;
   cudaError_t e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1012,6 +1016,22 @@ static cudaError_t tcg_set_attrs() {
     e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_VOCAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  for (int l = 0; l < 4 && e == cudaSuccess; ++l) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(1 << l));
+    cfg.blockDim = dim3(tcg::kThreads);
+    cfg.dynamicSmemBytes = tcg::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1u << l;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, tcg::tcg_kernel<tcg::GEPI_RESID>, &cfg);
+    g_tcg_clusters[l] = n;
+  }
   return e;
 }
 
@@ -1066,9 +1086,13 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
   const int wtiles = glu ? a.ms.n_pairs / (tcg::kWR / 2) : 2 * a.ms.n_pairs / tcg::kWR;
   const int items = wtiles * ((a.n + tcg::kAR - 1) / tcg::kAR);
   const int nks = a.K / 64;
-  // split K over a cluster while the tiles alone would leave SMs idle
-  int C = 1;
-  while (C < tcg::kMaxSplit && items * C * 2 <= sms && nks % (C * 2) == 0) C *= 2;
+  // split K over a cluster while the tiles alone would leave SMs idle and
+  // every cluster is resident at once (a second wave would double the time)
+  int C = 1, l = 0;
+  while (C < tcg::kMaxSplit && items * C * 2 <= sms && nks % (C * 2) == 0 && items <= g_tcg_clusters[l + 1]) {
+    C *= 2;
+    ++l;
+  }
   tcg::GMaps maps;
   memset(&maps, 0, sizeof(maps));
   int32_t rc;

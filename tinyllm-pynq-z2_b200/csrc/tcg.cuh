@@ -60,6 +60,8 @@ constexpr uint32_t kBT = kN * 128;    // bytes of an activation tile (one K step
 constexpr uint32_t kMS = kAT + kBT;   // 40960, a multiple of 1024
 constexpr uint32_t kPT = kWR * 48 * kG;  // packed bytes of a weight tile (one group of K steps)
 constexpr size_t kSmem = 1024 + (size_t)kS * kMS + (size_t)kP * kPT;
+// the partial tiles of every rank ([C][64 / C][128] floats) fit in the stage memory
+static_assert((size_t)kWR * kAR * 4 <= (size_t)kS * kMS, "partial tiles exceed the stages");
 
 enum { GEPI_QKV = 0, GEPI_RESID = 1, GEPI_GLU = 2, GEPI_VOCAB = 3 };
 
@@ -110,10 +112,12 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_constant__ GMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t pk_full[kP], pk_empty[kP], act_full[kS], a_full[kS], mma_empty[kS];
-  __shared__ uint64_t tmem_full, glu_ready, drain;
+  __shared__ uint64_t tmem_full, drain;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
-  __shared__ float glu_x[kWR / 2][kAR + 1];  // GLU: W3 values handed to the W1 lanes
+  __shared__ float srow[kWR];                 // row scales of the weight tile
+  __shared__ int32_t mflags[kAR], mpos[kAR], mseq[kAR], mgen[kAR], mplen[kAR];  // per activation
+  __shared__ unsigned long long vkey[kAR];    // VOCAB: this tile's first-maximum key per activation
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   constexpr bool kGlu = EPI == GEPI_GLU;
@@ -142,11 +146,11 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       mbar_init(mma_empty + s, 1);
     }
     mbar_init(&tmem_full, 1);
-    mbar_init(&glu_ready, kDW / 2);
     mbar_init(&drain, 1);
     abort_flag = 0;
     fence_mbar_init();
   }
+  if (EPI == GEPI_VOCAB && tid < kAR) vkey[tid] = 0ull;
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -226,6 +230,22 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
     // ---- warps 0-7: expand weights
     const int j = ((warp & 3) << 5) | lane;  // weight row this thread expands
     const int half = warp >> 2;               // units 2 half, 2 half + 1 of the step
+    // the epilogue's row scales and per-activation state, fetched while the
+    // first weight step is in flight (read after the cluster barriers below)
+    if (tid < kWR) {
+      int mi, r;
+      weight_row(a.ms, kGlu, wt, tid, mi, r);
+      srow[tid] = __ldg(scale_ptr(a.ms, mi) + r);
+    } else if (tid < kWR + kAR) {
+      const int al = tid - kWR, m = at * kAR + al;
+      const EpiArgs& ep = a.ep;
+      const bool in = m < a.n && (EPI == GEPI_QKV || EPI == GEPI_VOCAB);
+      mflags[al] = in ? ep.flags[m] : SEQ_INVALID;
+      mpos[al] = in && (EPI == GEPI_QKV || ep.step_logits) ? ep.pos[m] : 0;
+      mseq[al] = in && EPI == GEPI_QKV && ep.seq ? ep.seq[m] : m;
+      mgen[al] = in && EPI == GEPI_VOCAB && (ep.step_logits || ep.n_stop) ? ep.gen[m] : 0;
+      mplen[al] = in && EPI == GEPI_VOCAB && ep.step_logits ? ep.plen[m] : 0;
+    }
     for (int g = 0; g < nk; ++g) {
       const int p = g % kP, s = g % kS;
       bool got = !abort_flag && mbar_wait(pk_full + p, (g / kP) & 1);
@@ -261,14 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   }
 
   // ---- partial tile -> the shared memory of the CTA that owns each activation
-  // slice: CTA q receives, for activations [q SA, (q+1) SA), one slot per rank
-  // (stage memory, free once this CTA's MMAs are done; a peer writes into it
-  // only after its own K loop, and every CTA's MMAs finish before the barrier)
-  const int SA = kAR / C, SH = SA / 2;
-  float* recv = reinterpret_cast<float*>(smem);  // [C ranks][128 rows][SA]
-  const int j = ((warp & 3) << 5) | lane;
-  const int half = (warp >> 2) & 1;
-  // every CTA's MMAs are done before any peer writes into its stage memory
+  // slice: CTA q receives, for activations [q SA, (q+1) SA), one [SA][128]
+  // slot per rank (stage memory, free once this CTA's MMAs are done; a peer
+  // writes into it only after its own K loop, and every CTA's MMAs finish
+  // before the barrier).  A warp's 32 rows are 32 consecutive words.
+  const int SA = kAR / C;
+  float* recv = reinterpret_cast<float*>(smem);  // [C ranks][SA activations][128 rows]
   if (warp < kDW) {
     const bool full = __all_sync(0xffffffffu, !abort_flag && mbar_wait(&tmem_full, 0));
     if (!full && lane == 0) {
@@ -280,150 +298,97 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   cl.sync();
   if (warp < kDW) {
     tc::tc_fence_after();
+    const int j = ((warp & 3) << 5) | lane;
+    const int half = warp >> 2;
     const uint32_t lane_addr = taddr + ((uint32_t)((warp & 3) * 32) << 16);
-    float d0[32], d1[32], d2[32];
-    tc::tmem_ld32(lane_addr + half * 32, d0);
-    tc::tmem_ld32(lane_addr + kAR + half * 32, d1);
-    tc::tmem_ld32(lane_addr + 2 * kAR + half * 32, d2);
+    // parts summed in order (hi + mid) + lo, one part held at a time
+    float d[32], e[32];
+    tc::tmem_ld32(lane_addr + half * 32, d);
+    tc::tmem_ld32(lane_addr + kAR + half * 32, e);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) d[i] = __fadd_rn(d[i], e[i]);
+    tc::tmem_ld32(lane_addr + 2 * kAR + half * 32, e);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int la = half * 32 + i;  // local activation
       const int q = la / SA;         // owner rank
       float* dst = C == 1 ? recv : cl.map_shared_rank(recv, q);
-      dst[((size_t)c * kWR + j) * SA + (la - q * SA)] = __fadd_rn(__fadd_rn(d0[i], d1[i]), d2[i]);
+      dst[(c * SA + la - q * SA) * kWR + j] = __fadd_rn(d[i], e[i]);
     }
   }
   tc::tc_fence_before();
   cl.sync();  // every partial has landed in its owner
 
-  // ---- this CTA's activations: [c SA, (c+1) SA); warps w, w+4 take halves
+  // ---- epilogue of activations [c SA, (c+1) SA): thread t takes row pair
+  // t % 64 ((2p, 2p+1), or (W1 row p, W3 row p) in GLU mode) of activations
+  // t / 64, t / 64 + 4, ...; a warp works on one activation at a time and
+  // its stores are contiguous.  The loop is kept rolled: straight-line code
+  // run once per CTA is bound by instruction fetch.
   if (warp < kDW) {
-    int mi, r;
-    weight_row(a.ms, kGlu, wt, j, mi, r);
-    const float scale = __ldg(scale_ptr(a.ms, mi) + r);
-    const int a0 = at * kAR + c * SA + half * SH;  // global activation row of y[0]
-    float y[kAR / 2];
-#pragma unroll
-    for (int i = 0; i < kAR / 2; ++i) {
-      float v = 0.f;
-      if (i < SH)
-        for (int q = 0; q < C; ++q) {  // rank order: one summation order everywhere
-          const float pv = recv[((size_t)q * kWR + j) * SA + half * SH + i];
-          v = q == 0 ? pv : __fadd_rn(v, pv);
-        }
-      y[i] = __fmul_rn(v, scale);
-    }
     const EpiArgs& ep = a.ep;
-    if (EPI == GEPI_GLU) {
-      // rows 64..127 (warps 2, 3, 6, 7) hold W3: hand them to the W1 rows
-      if (j >= kWR / 2) {
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i)
-          if (i < SH) glu_x[j - kWR / 2][half * SH + i] = y[i];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&glu_ready);
-      } else if (__all_sync(0xffffffffu, mbar_wait(&glu_ready, 0))) {
-        const int p = wt * (kWR / 2) + j;
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i)
-          if (i < SH && a0 + i < a.n) epilogue<EPI_GLU>(ep, a0 + i, p, y[i], glu_x[j][half * SH + i]);
-      } else if (lane == 0) {
-        atomicOr(a.err, tc::kErrTimeout);
+    const int pp = tid & (kWR / 2 - 1), as = tid >> 6;
+    const int r0 = kGlu ? pp : 2 * pp, r1 = kGlu ? pp + kWR / 2 : 2 * pp + 1;
+    const float s0 = srow[r0], s1 = srow[r1];
+    const int vrow = wt * kWR + 2 * pp;  // non-GLU: global row of the pair's first value
+#pragma unroll 2
+    for (int al = as; al < SA; al += kDW / 2) {
+      float v0 = 0.f, v1 = 0.f;
+      for (int q = 0; q < C; ++q) {  // rank order: one summation order everywhere
+        const float* src = recv + (size_t)(q * SA + al) * kWR;
+        const float p0 = src[r0], p1 = src[r1];
+        v0 = q == 0 ? p0 : __fadd_rn(v0, p0);
+        v1 = q == 0 ? p1 : __fadd_rn(v1, p1);
       }
-    } else {
-      // pairs (2p, 2p+1) sit on adjacent lanes; the even lane finishes the pair.
-      // Every global value needed is loaded for all of the thread's activations
-      // before any store, so the loads overlap.
-      const int vrow = wt * kWR + j;
-      const bool lead = !(j & 1);
-      float other[kAR / 2];
-#pragma unroll
-      for (int i = 0; i < kAR / 2; ++i) other[i] = __shfl_xor_sync(0xffffffffu, y[i], 1);
-      if (EPI == GEPI_RESID) {
-        float2 old[kAR / 2];
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i)
-          old[i] = i < SH && lead && a0 + i < a.n
-                       ? *reinterpret_cast<const float2*>(ep.y + (int64_t)(a0 + i) * ep.ldy + vrow)
-                       : make_float2(0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i)
-          if (i < SH && lead && a0 + i < a.n)
-            *reinterpret_cast<float2*>(ep.y + (int64_t)(a0 + i) * ep.ldy + vrow) =
-                make_float2(__fadd_rn(old[i].x, y[i]), __fadd_rn(old[i].y, other[i]));
+      v0 = __fmul_rn(v0, s0);
+      v1 = __fmul_rn(v1, s1);
+      const int ml = c * SA + al, m = at * kAR + ml;
+      if (EPI == GEPI_GLU) {
+        if (m < a.n) ep.y[(int64_t)m * ep.ldy + wt * (kWR / 2) + pp] = swiglu(v0, v1);
+      } else if (EPI == GEPI_RESID) {
+        // the only writer of this element: one rounded add onto the residual
+        if (m < a.n) atomicAdd(reinterpret_cast<float2*>(ep.y + (int64_t)m * ep.ldy + vrow), make_float2(v0, v1));
       } else if (EPI == GEPI_QKV) {
         // RoPE of torch_benchmark.py:84 (each product rounded before the add);
         // q to the query buffer, k and v to the cache row of the activation's sequence
-        const bool rope = vrow < ep.q_rows + ep.kv_rows;
-        const int jr = (vrow % ep.hd) >> 1;
-        int pos[kAR / 2];
-        int64_t crow[kAR / 2];
-        bool live[kAR / 2];
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i) {
-          const int m = a0 + i;
-          live[i] = i < SH && lead && m < a.n && !(ep.flags[m] & SEQ_INVALID);
-          pos[i] = live[i] ? ep.pos[m] : 0;
-          crow[i] = live[i] && ep.seq ? ep.seq[m] : m;
-        }
-        float cs[kAR / 2], sn[kAR / 2];
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i) {
-          cs[i] = live[i] && rope ? __ldg(ep.rope_cos + (int64_t)pos[i] * (ep.hd >> 1) + jr) : 0.f;
-          sn[i] = live[i] && rope ? __ldg(ep.rope_sin + (int64_t)pos[i] * (ep.hd >> 1) + jr) : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i) {
-          if (!live[i]) continue;
-          float ra = y[i], rb = other[i];
-          if (rope) {
-            ra = __fsub_rn(__fmul_rn(y[i], cs[i]), __fmul_rn(other[i], sn[i]));
-            rb = __fadd_rn(__fmul_rn(y[i], sn[i]), __fmul_rn(other[i], cs[i]));
+        if (m < a.n && !(mflags[ml] & SEQ_INVALID)) {
+          const int pos = mpos[ml];
+          const int64_t crow = mseq[ml];
+          float ra = v0, rb = v1;
+          if (vrow < ep.q_rows + ep.kv_rows) {
+            const int jr = (vrow % ep.hd) >> 1;
+            const float cs = __ldg(ep.rope_cos + (int64_t)pos * (ep.hd >> 1) + jr);
+            const float sn = __ldg(ep.rope_sin + (int64_t)pos * (ep.hd >> 1) + jr);
+            ra = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
+            rb = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
           }
           float* dst;
           if (vrow < ep.q_rows)
-            dst = ep.qbuf + (int64_t)(a0 + i) * ep.ldq + vrow;
+            dst = ep.qbuf + (int64_t)m * ep.ldq + vrow;
           else if (vrow < ep.q_rows + ep.kv_rows)
-            dst = ep.kc + crow[i] * ep.cache_stride + ep.layer_off + (int64_t)pos[i] * ep.kv_rows + (vrow - ep.q_rows);
+            dst = ep.kc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (vrow - ep.q_rows);
           else
-            dst = ep.vc + crow[i] * ep.cache_stride + ep.layer_off + (int64_t)pos[i] * ep.kv_rows +
+            dst = ep.vc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
                   (vrow - ep.q_rows - ep.kv_rows);
           *reinterpret_cast<float2*>(dst) = make_float2(ra, rb);
         }
       } else {  // GEPI_VOCAB: logits, dumped step logits, stop masking, first-maximum key
-        int gen[kAR / 2], fl[kAR / 2], pos[kAR / 2], plen[kAR / 2];
-        const bool need = ep.step_logits || ep.n_stop;
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i) {
-          const int m = a0 + i;
-          const bool in = need && i < SH && lead && m < a.n;
-          gen[i] = in ? ep.gen[m] : 0;
-          fl[i] = in ? ep.flags[m] : 0;
-          pos[i] = in && ep.step_logits ? ep.pos[m] : 0;
-          plen[i] = in && ep.step_logits ? ep.plen[m] : 0;
-        }
-#pragma unroll
-        for (int i = 0; i < kAR / 2; ++i) {
-          if (i >= SH) break;
-          const int m = a0 + i;
-          unsigned long long key = 0ull;
-          if (lead && m < a.n) {
-            float va = y[i], vb = other[i];
-            if (ep.y) *reinterpret_cast<float2*>(ep.y + (int64_t)m * ep.ldy + vrow) = make_float2(va, vb);
-            if (ep.step_logits && !(fl[i] & (SEQ_DONE | SEQ_INVALID)) && pos[i] >= plen[i] - 1)
-              *reinterpret_cast<float2*>(ep.step_logits + ((int64_t)m * ep.new_tokens + gen[i]) * ep.vocab + vrow) =
-                  make_float2(va, vb);
-            if (ep.n_stop && gen[i] < ep.min_new) {
-              for (int t = 0; t < ep.n_stop; ++t) {
-                if (ep.stop_ids[t] == vrow) va = -INFINITY;
-                if (ep.stop_ids[t] == vrow + 1) vb = -INFINITY;
-              }
+        if (m < a.n) {  // warp-uniform: a warp holds one activation
+          float va = v0, vb = v1;
+          const int gen = mgen[ml];
+          if (ep.y) *reinterpret_cast<float2*>(ep.y + (int64_t)m * ep.ldy + vrow) = make_float2(va, vb);
+          if (ep.step_logits && !(mflags[ml] & (SEQ_DONE | SEQ_INVALID)) && mpos[ml] >= mplen[ml] - 1)
+            *reinterpret_cast<float2*>(ep.step_logits + ((int64_t)m * ep.new_tokens + gen) * ep.vocab + vrow) =
+                make_float2(va, vb);
+          if (ep.n_stop && gen < ep.min_new) {
+            for (int t = 0; t < ep.n_stop; ++t) {
+              if (ep.stop_ids[t] == vrow) va = -INFINITY;
+              if (ep.stop_ids[t] == vrow + 1) vb = -INFINITY;
             }
-            key = umax64(argmax_key(va, vrow), argmax_key(vb, vrow + 1));
           }
+          unsigned long long key = umax64(argmax_key(va, vrow), argmax_key(vb, vrow + 1));
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) key = umax64(key, __shfl_xor_sync(0xffffffffu, key, o));
-          if (lane == 0 && key && m < a.n) atomicMax(ep.keys + m, key);
+          if (lane == 0) atomicMax(vkey + ml, key);
         }
       }
     }
@@ -434,6 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
     tc::tc_fence_after();
     tc::tmem_dealloc(taddr, 256);
   }
+  // one global atomic per (tile, activation) instead of one per warp
+  if (EPI == GEPI_VOCAB && tid < kAR && vkey[tid]) atomicMax(a.ep.keys + at * kAR + tid, vkey[tid]);
 }
 
 // Activation image (tc.cuh layout, K columns) of rows x[0..n): RMSNorm with
