@@ -10,13 +10,16 @@
 // sum_k q_k u_k with exact bf16 products and FP32 accumulation (the parts hold
 // u's 24-bit significand), times the row scale once.
 //
-// Two rings, per K step of 64 columns (one 128-byte swizzle atom):
+// Three rings, per K step of 64 columns (one 128-byte swizzle atom):
 //  * packed weights: the 128 rows x 48 bytes of int6 codes of a K step arrive
 //    by one 2-D TMA tensor load (no multicast; two 64-row boxes in GLU mode),
-//    6 steps deep;
-//  * MMA stages (4): the weight rows expanded to bf16 by the decode warps
-//    (16 KB) and the 192 activation rows, bulk-copied from the pre-swizzled
-//    activation image (24 KB).
+//    8 steps deep;
+//  * expanded weights (4 stages) in tensor memory: the decode warps write the
+//    bf16 rows with tcgen05.st (row r on TMEM lane r, K elements 2e, 2e+1 in
+//    column e) and the MMA reads its A operand from there, so the expansion
+//    costs no shared-memory bandwidth;
+//  * activations (6 stages): the 192 rows of a K step, bulk-copied from the
+//    pre-swizzled activation image (24 KB), the MMA's B operand.
 // Split K.  A matrix with few tiles (wq|wk|wv, wo, w2 of the 1.1B shape: 16-20
 // tiles of 128 rows) would occupy 16-20 SMs; instead a thread-block cluster of
 // C CTAs (C = 2, 4 or 8) shares one tile, each CTA taking K steps
@@ -46,22 +49,24 @@ namespace tcg {
 constexpr int kWR = 128;          // weight rows per tile (MMA M)
 constexpr int kAR = 64;           // activation rows per tile (x 3 parts = MMA N)
 constexpr int kN = 3 * kAR;       // 192
-constexpr int kS = 4;             // MMA stages
+constexpr int kS = 6;             // activation stages (shared memory)
+constexpr int kSA = 4;            // expanded-weight stages (tensor memory, 32 columns each)
 constexpr int kMaxSplit = 8;      // CTAs of a cluster splitting one tile's K range
 constexpr int kG = 1;             // K steps per packed-weight group (one TMA box)
-constexpr int kP = 6;             // packed-weight groups in the ring
+constexpr int kP = 8;             // packed-weight groups in the ring
 // Boxes wider than 128 bytes per row (kG > 2) delivered wrong bytes in the
 // parity tests here; 48 and 96 bytes were exact and equally fast.
 static_assert(48 * kG <= 128, "TMA box rows of at most 128 bytes");
 constexpr int kThreads = 320;     // 10 warps
 constexpr int kDW = 8;            // expand / epilogue warps
-constexpr uint32_t kAT = kWR * 128;   // bytes of a decoded weight tile (one K step)
 constexpr uint32_t kBT = kN * 128;    // bytes of an activation tile (one K step)
-constexpr uint32_t kMS = kAT + kBT;   // 40960, a multiple of 1024
+constexpr uint32_t kTmemCols = 512;   // accumulator [0, 192), weight stages from kAcol
+constexpr uint32_t kAcol = 256;
+static_assert(kAcol + 32 * kSA <= kTmemCols && kN <= kAcol, "tensor memory columns");
 constexpr uint32_t kPT = kWR * 48 * kG;  // packed bytes of a weight tile (one group of K steps)
-constexpr size_t kSmem = 1024 + (size_t)kS * kMS + (size_t)kP * kPT;
+constexpr size_t kSmem = 1024 + (size_t)kS * kBT + (size_t)kP * kPT;
 // the partial tiles of every rank ([C][64 / C][128] floats) fit in the stage memory
-static_assert((size_t)kWR * kAR * 4 <= (size_t)kS * kMS, "partial tiles exceed the stages");
+static_assert((size_t)kWR * kAR * 4 <= (size_t)kS * kBT, "partial tiles exceed the stages");
 
 enum { GEPI_QKV = 0, GEPI_RESID = 1, GEPI_GLU = 2, GEPI_VOCAB = 3 };
 
@@ -111,7 +116,7 @@ __device__ __forceinline__ const float* scale_ptr(const MatSet& ms, int mi) {
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_constant__ GMaps maps) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t pk_full[kP], pk_empty[kP], act_full[kS], a_full[kS], mma_empty[kS];
+  __shared__ uint64_t pk_full[kP], pk_empty[kP], act_full[kS], act_empty[kS], a_full[kSA], a_empty[kSA];
   __shared__ uint64_t tmem_full, drain;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
@@ -123,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   constexpr bool kGlu = EPI == GEPI_GLU;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* packed = smem + (size_t)kS * kMS;
+  uint8_t* packed = smem + (size_t)kS * kBT;
   const int C = (int)cl.num_blocks(), c = (int)cl.block_rank();
   const int nks = a.K / 64;
   const int wtiles = kGlu ? a.ms.n_pairs / (kWR / 2) : (2 * a.ms.n_pairs) / kWR;
@@ -132,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   const int ks0 = c * (nks / C), nk = nks / C;  // this CTA's K steps
 
   if (warp == kDW + 1) {
-    tc::tmem_alloc(&tmem_base, 256);
+    tc::tmem_alloc(&tmem_base, kTmemCols);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
@@ -142,8 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
     }
     for (int s = 0; s < kS; ++s) {
       mbar_init(act_full + s, 1);
+      mbar_init(act_empty + s, 1);
+    }
+    for (int s = 0; s < kSA; ++s) {
       mbar_init(a_full + s, kDW);
-      mbar_init(mma_empty + s, 1);
+      mbar_init(a_empty + s, 1);
     }
     mbar_init(&tmem_full, 1);
     mbar_init(&drain, 1);
@@ -184,12 +192,12 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       const uint8_t* isrc = a.img + (arow >> 7) * (3 * (int64_t)a.K * 256) + (arow & 127) * 128;
       for (int g = 0; g < nk && !abort_flag; ++g) {
         const int s = g % kS;
-        if (g >= kS && !mbar_wait(mma_empty + s, ((g / kS) - 1) & 1)) {
+        if (g >= kS && !mbar_wait(act_empty + s, ((g / kS) - 1) & 1)) {
           abort_flag = 1;
           atomicOr(a.err, tc::kErrTimeout);
           break;
         }
-        uint8_t* st = smem + (size_t)s * kMS + kAT;
+        uint8_t* st = smem + (size_t)s * kBT;
         mbar_expect_tx(act_full + s, kBT);
 #pragma unroll
         for (int p = 0; p < 3; ++p)
@@ -204,17 +212,19 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
                              ((uint32_t)(kWR >> 4) << 24);
       bool ok = true;
       for (int g = 0; g < nk && !abort_flag; ++g) {
-        const int s = g % kS;
-        if (!mbar_wait(act_full + s, (g / kS) & 1) || !mbar_wait(a_full + s, (g / kS) & 1)) {
+        const int s = g % kS, sa = g % kSA;
+        if (!mbar_wait(act_full + s, (g / kS) & 1) || !mbar_wait(a_full + sa, (g / kSA) & 1)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + (size_t)s * kMS), b0 = a0 + kAT;
+        const uint32_t b0 = smem_u32(smem + (size_t)s * kBT);
+        const uint32_t a0 = taddr + kAcol + 32 * sa;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tc::umma(taddr, tc::sdesc(a0 + kk * 32), tc::sdesc(b0 + kk * 32), idesc, (g | kk) != 0);
-        tc::umma_commit(mma_empty + s);
+          tc::umma_ts(taddr, a0 + 8 * kk, tc::sdesc(b0 + kk * 32), idesc, (g | kk) != 0);
+        tc::umma_commit(act_empty + s);
+        tc::umma_commit(a_empty + sa);
       }
       if (!ok) {
         abort_flag = 1;
@@ -246,37 +256,38 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       mgen[al] = in && EPI == GEPI_VOCAB && (ep.step_logits || ep.n_stop) ? ep.gen[m] : 0;
       mplen[al] = in && EPI == GEPI_VOCAB && ep.step_logits ? ep.plen[m] : 0;
     }
+    // this thread's TMEM lane (row j), columns 16 half .. 16 half + 15 of a stage
+    const uint32_t a_lane = taddr + ((uint32_t)((warp & 3) * 32) << 16) + kAcol + 16 * half;
     for (int g = 0; g < nk; ++g) {
-      const int p = g % kP, s = g % kS;
+      const int p = g % kP, sa = g % kSA;
       bool got = !abort_flag && mbar_wait(pk_full + p, (g / kP) & 1);
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the warp leaves together
       const uint2* pp = reinterpret_cast<const uint2*>(packed + (size_t)p * kPT + j * 48 + half * 24);
       const uint2 p0 = pp[0], p1 = pp[1], p2 = pp[2];
       __syncwarp();
       if (lane == 0) mbar_arrive(pk_empty + p);  // the packed step is in registers
-      // the MMA of this stage's previous use has finished reading its weight tile
-      got = g < kS || mbar_wait(mma_empty + s, ((g / kS) - 1) & 1);
+      // the MMAs of this weight stage's previous use have finished reading it
+      got = g < kSA || mbar_wait(a_empty + sa, ((g / kSA) - 1) & 1);
       if (!__all_sync(0xffffffffu, got)) break;
+      tc::tc_fence_after();
       const uint32_t w[6] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y};
-      uint8_t* line = smem + (size_t)s * kMS + j * 128;
+      uint32_t pk[16];  // column e: K elements (2e, 2e+1) of the thread's 32
 #pragma unroll
       for (int uu = 0; uu < 2; ++uu) {
         const uint32_t w0 = w[3 * uu], w1 = w[3 * uu + 1], w2 = w[3 * uu + 2];
         const uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
                                 w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
                                 w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
-        uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          pk[e] = (__float_as_uint(code_to_float(f[2 * e])) >> 16) |
-                  (__float_as_uint(code_to_float(f[2 * e + 1])) & 0xFFFF0000u);
-        const int lu = 2 * (2 * half + uu);
-        reinterpret_cast<uint4*>(line)[lu ^ (j & 7)] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        reinterpret_cast<uint4*>(line)[(lu + 1) ^ (j & 7)] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          pk[8 * uu + e] = (__float_as_uint(code_to_float(f[2 * e])) >> 16) |
+                           (__float_as_uint(code_to_float(f[2 * e + 1])) & 0xFFFF0000u);
       }
-      tc::fence_async_smem();
+      tc::tmem_st16(a_lane + 32 * sa, pk);
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(a_full + s);
+      if (lane == 0) mbar_arrive(a_full + sa);
     }
   }
 
@@ -397,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   __syncthreads();
   if (warp == kDW + 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(taddr, 256);
+    tc::tmem_dealloc(taddr, kTmemCols);
   }
   // one global atomic per (tile, activation) instead of one per warp
   if (EPI == GEPI_VOCAB && tid < kAR && vkey[tid]) atomicMax(a.ep.keys + at * kAR + tid, vkey[tid]);
