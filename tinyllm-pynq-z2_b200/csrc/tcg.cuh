@@ -31,9 +31,10 @@
 // epilogue for them.  No multicast.
 // Warps 0-7 expand (warps w and w+4 take the two halves of row 32(w%4)+lane)
 // and later run the epilogue (TMEM lane quadrant w%4; warps 0-3 activations
-// 0-31, warps 4-7 activations 32-63), warp 8 issues the copies (lane 0 the
-// weight loads, lane 1 the activation loads), warp 9 issues the MMAs and owns
-// TMEM.  Every wait is bounded; a timeout sets an error bit and the CTA stops.
+// 0-31, warps 4-7 activations 32-63), warp 8 issues the weight loads, warp
+// 9 the MMAs (and owns TMEM), warp 10 the activation loads: each waiting role
+// has a warp of its own, so no role's wait holds up another's issue.
+// Every wait is bounded; a timeout sets an error bit and the CTA stops.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -57,7 +58,7 @@ constexpr int kP = 8;             // packed-weight groups in the ring
 // Boxes wider than 128 bytes per row (kG > 2) delivered wrong bytes in the
 // parity tests here; 48 and 96 bytes were exact and equally fast.
 static_assert(48 * kG <= 128, "TMA box rows of at most 128 bytes");
-constexpr int kThreads = 320;     // 10 warps
+constexpr int kThreads = 352;     // 11 warps
 constexpr int kDW = 8;            // expand / epilogue warps
 constexpr uint32_t kBT = kN * 128;    // bytes of an activation tile (one K step)
 constexpr uint32_t kTmemCols = 512;   // accumulator [0, 192), weight stages from kAcol
@@ -186,7 +187,9 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
           tma_load_2d(dst, &maps.m[mi], x, r0, pk_full + p);
         }
       }
-    } else if (lane == 1) {
+    }
+  } else if (warp == kDW + 2) {
+    if (lane == 0) {
       // ---- activation loads: 3 bulk copies (one per part) per K step
       const int64_t arow = (int64_t)at * kAR;
       const uint8_t* isrc = a.img + (arow >> 7) * (3 * (int64_t)a.K * 256) + (arow & 127) * 128;
