@@ -1085,7 +1085,7 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
   const bool glu = epi == tcg::GEPI_GLU;
   const int wtiles = glu ? a.ms.n_pairs / (tcg::kWR / 2) : 2 * a.ms.n_pairs / tcg::kWR;
   const int items = wtiles * ((a.n + tcg::kAR - 1) / tcg::kAR);
-  const int nks = a.K / 64;
+  const int nks = a.K / (64 * tcg::kG);  // K steps
   // split K over a cluster while the tiles alone would leave SMs idle and
   // every cluster is resident at once (a second wave would double the time)
   int C = 1, l = 0;

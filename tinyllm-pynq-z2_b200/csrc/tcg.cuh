@@ -10,16 +10,19 @@
 // sum_k q_k u_k with exact bf16 products and FP32 accumulation (the parts hold
 // u's 24-bit significand), times the row scale once.
 //
-// Three rings, per K step of 64 columns (one 128-byte swizzle atom):
-//  * packed weights: the 128 rows x 48 bytes of int6 codes of a K step arrive
+// Per K step of 128 columns (two 128-byte swizzle atoms), three rings:
+//  * packed weights: the 128 rows x 96 bytes of int6 codes of a K step arrive
 //    by one 2-D TMA tensor load (no multicast; two 64-row boxes in GLU mode),
-//    8 steps deep;
-//  * expanded weights (4 stages) in tensor memory: the decode warps write the
-//    bf16 rows with tcgen05.st (row r on TMEM lane r, K elements 2e, 2e+1 in
-//    column e) and the MMA reads its A operand from there, so the expansion
-//    costs no shared-memory bandwidth;
-//  * activations (6 stages): the 192 rows of a K step, bulk-copied from the
-//    pre-swizzled activation image (24 KB), the MMA's B operand.
+//    6 steps deep;
+//  * expanded weights (3 stages of 64 columns) in tensor memory: the decode
+//    warps write the bf16 rows with tcgen05.st (row r on TMEM lane r, K
+//    elements 2e, 2e+1 in column e) and the MMA reads its A operand from
+//    there, so the expansion costs no shared-memory bandwidth;
+//  * activations (3 stages of 48 KB): the 192 rows of both 64-column chunks,
+//    bulk-copied from the pre-swizzled activation image, the MMA's B operand.
+// One commit per step frees a weight stage and an activation stage together.
+// Every K step pays a fixed handshake latency (barrier waits and arrivals,
+// the commit); 128 columns a step halve its share against 64.
 // Split K.  A matrix with few tiles (wq|wk|wv, wo, w2 of the 1.1B shape: 16-20
 // tiles of 128 rows) would occupy 16-20 SMs; instead a thread-block cluster of
 // C CTAs (C = 2, 4 or 8) shares one tile, each CTA taking K steps
@@ -50,20 +53,20 @@ namespace tcg {
 constexpr int kWR = 128;          // weight rows per tile (MMA M)
 constexpr int kAR = 64;           // activation rows per tile (x 3 parts = MMA N)
 constexpr int kN = 3 * kAR;       // 192
-constexpr int kS = 6;             // activation stages (shared memory)
-constexpr int kSA = 4;            // expanded-weight stages (tensor memory, 32 columns each)
+constexpr int kG = 2;             // 64-column chunks per K step (one TMA box of 48 kG bytes a row)
+constexpr int kS = 3;             // K-step stages: activations (shared memory) + expanded weights (TMEM)
 constexpr int kMaxSplit = 8;      // CTAs of a cluster splitting one tile's K range
-constexpr int kG = 1;             // K steps per packed-weight group (one TMA box)
-constexpr int kP = 8;             // packed-weight groups in the ring
+constexpr int kP = 6;             // packed-weight K steps in the ring
 // Boxes wider than 128 bytes per row (kG > 2) delivered wrong bytes in the
-// parity tests here; 48 and 96 bytes were exact and equally fast.
+// parity tests here; 48 and 96 bytes were exact.
 static_assert(48 * kG <= 128, "TMA box rows of at most 128 bytes");
 constexpr int kThreads = 352;     // 11 warps
 constexpr int kDW = 8;            // expand / epilogue warps
-constexpr uint32_t kBT = kN * 128;    // bytes of an activation tile (one K step)
-constexpr uint32_t kTmemCols = 512;   // accumulator [0, 192), weight stages from kAcol
+constexpr uint32_t kBT = kG * kN * 128;  // activation bytes of a K step: [chunk][part][64 rows][128 B]
+constexpr uint32_t kTmemCols = 512;      // accumulator [0, 192), weight stages from kAcol
 constexpr uint32_t kAcol = 256;
-static_assert(kAcol + 32 * kSA <= kTmemCols && kN <= kAcol, "tensor memory columns");
+constexpr uint32_t kAS = 32 * kG;        // TMEM columns of an expanded weight stage
+static_assert(kAcol + kAS * kS <= kTmemCols && kN <= kAcol, "tensor memory columns");
 constexpr uint32_t kPT = kWR * 48 * kG;  // packed bytes of a weight tile (one group of K steps)
 constexpr size_t kSmem = 1024 + (size_t)kS * kBT + (size_t)kP * kPT;
 // the partial tiles of every rank ([C][64 / C][128] floats) fit in the stage memory
@@ -117,7 +120,7 @@ __device__ __forceinline__ const float* scale_ptr(const MatSet& ms, int mi) {
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_constant__ GMaps maps) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t pk_full[kP], pk_empty[kP], act_full[kS], act_empty[kS], a_full[kSA], a_empty[kSA];
+  __shared__ uint64_t pk_full[kP], pk_empty[kP], act_full[kS], a_full[kS], st_empty[kS];
   __shared__ uint64_t tmem_full, drain;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* packed = smem + (size_t)kS * kBT;
   const int C = (int)cl.num_blocks(), c = (int)cl.block_rank();
-  const int nks = a.K / 64;
+  const int nks = a.K / (64 * kG);
   const int wtiles = kGlu ? a.ms.n_pairs / (kWR / 2) : (2 * a.ms.n_pairs) / kWR;
   const int it = blockIdx.x / C;  // one item (weight tile, activation tile) per cluster
   const int wt = it % wtiles, at = it / wtiles;
@@ -148,11 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
     }
     for (int s = 0; s < kS; ++s) {
       mbar_init(act_full + s, 1);
-      mbar_init(act_empty + s, 1);
-    }
-    for (int s = 0; s < kSA; ++s) {
       mbar_init(a_full + s, kDW);
-      mbar_init(a_empty + s, 1);
+      mbar_init(st_empty + s, 1);
     }
     mbar_init(&tmem_full, 1);
     mbar_init(&drain, 1);
@@ -178,11 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
           break;
         }
         uint8_t* dst = packed + (size_t)p * kPT;
-        const int x = (ks0 + g) * 48;
+        const int x = (ks0 + g) * 48 * kG;
         mbar_expect_tx(pk_full + p, kPT);
         if (kGlu) {
           tma_load_2d(dst, &maps.m[0], x, r0, pk_full + p);
-          tma_load_2d(dst + (kWR / 2) * 48, &maps.m[1], x, r0, pk_full + p);
+          tma_load_2d(dst + (kWR / 2) * 48 * kG, &maps.m[1], x, r0, pk_full + p);
         } else {
           tma_load_2d(dst, &maps.m[mi], x, r0, pk_full + p);
         }
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       const uint8_t* isrc = a.img + (arow >> 7) * (3 * (int64_t)a.K * 256) + (arow & 127) * 128;
       for (int g = 0; g < nk && !abort_flag; ++g) {
         const int s = g % kS;
-        if (g >= kS && !mbar_wait(act_empty + s, ((g / kS) - 1) & 1)) {
+        if (g >= kS && !mbar_wait(st_empty + s, ((g / kS) - 1) & 1)) {
           abort_flag = 1;
           atomicOr(a.err, tc::kErrTimeout);
           break;
@@ -203,9 +203,11 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
         uint8_t* st = smem + (size_t)s * kBT;
         mbar_expect_tx(act_full + s, kBT);
 #pragma unroll
-        for (int p = 0; p < 3; ++p)
-          bulk_g2s(st + p * (kAR * 128), isrc + (int64_t)p * a.K * 256 + (int64_t)(ks0 + g) * 16384, kAR * 128,
-                   act_full + s);
+        for (int h = 0; h < kG; ++h)
+#pragma unroll
+          for (int p = 0; p < 3; ++p)
+            bulk_g2s(st + (h * 3 + p) * (kAR * 128),
+                     isrc + (int64_t)p * a.K * 256 + (int64_t)((ks0 + g) * kG + h) * 16384, kAR * 128, act_full + s);
       }
     }
   } else if (warp == kDW + 1) {
@@ -215,19 +217,19 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
                              ((uint32_t)(kWR >> 4) << 24);
       bool ok = true;
       for (int g = 0; g < nk && !abort_flag; ++g) {
-        const int s = g % kS, sa = g % kSA;
-        if (!mbar_wait(act_full + s, (g / kS) & 1) || !mbar_wait(a_full + sa, (g / kSA) & 1)) {
+        const int s = g % kS;
+        if (!mbar_wait(act_full + s, (g / kS) & 1) || !mbar_wait(a_full + s, (g / kS) & 1)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
         const uint32_t b0 = smem_u32(smem + (size_t)s * kBT);
-        const uint32_t a0 = taddr + kAcol + 32 * sa;
+        const uint32_t a0 = taddr + kAcol + kAS * s;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::umma_ts(taddr, a0 + 8 * kk, tc::sdesc(b0 + kk * 32), idesc, (g | kk) != 0);
-        tc::umma_commit(act_empty + s);
-        tc::umma_commit(a_empty + sa);
+        for (int kk = 0; kk < 4 * kG; ++kk)
+          tc::umma_ts(taddr, a0 + 8 * kk, tc::sdesc(b0 + (kk >> 2) * (3 * kAR * 128) + (kk & 3) * 32), idesc,
+                      (g | kk) != 0);
+        tc::umma_commit(st_empty + s);  // frees the activation stage and the weight stage
       }
       if (!ok) {
         abort_flag = 1;
@@ -259,38 +261,49 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       mgen[al] = in && EPI == GEPI_VOCAB && (ep.step_logits || ep.n_stop) ? ep.gen[m] : 0;
       mplen[al] = in && EPI == GEPI_VOCAB && ep.step_logits ? ep.plen[m] : 0;
     }
-    // this thread's TMEM lane (row j), columns 16 half .. 16 half + 15 of a stage
-    const uint32_t a_lane = taddr + ((uint32_t)((warp & 3) * 32) << 16) + kAcol + 16 * half;
+    // this thread's TMEM lane (row j), columns [16 kG half, 16 kG (half + 1)) of a stage:
+    // K elements [32 kG half, 32 kG (half + 1)) of the step, bytes [24 kG half, +24 kG) of the row
+    const uint32_t a_lane = taddr + ((uint32_t)((warp & 3) * 32) << 16) + kAcol + 16 * kG * half;
     for (int g = 0; g < nk; ++g) {
-      const int p = g % kP, sa = g % kSA;
+      const int p = g % kP, s = g % kS;
       bool got = !abort_flag && mbar_wait(pk_full + p, (g / kP) & 1);
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: the warp leaves together
-      const uint2* pp = reinterpret_cast<const uint2*>(packed + (size_t)p * kPT + j * 48 + half * 24);
-      const uint2 p0 = pp[0], p1 = pp[1], p2 = pp[2];
+      uint32_t w[6 * kG];
+      {
+        const uint2* pp = reinterpret_cast<const uint2*>(packed + (size_t)p * kPT + j * 48 * kG + half * 24 * kG);
+#pragma unroll
+        for (int i = 0; i < 3 * kG; ++i) {
+          const uint2 v = pp[i];
+          w[2 * i] = v.x;
+          w[2 * i + 1] = v.y;
+        }
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(pk_empty + p);  // the packed step is in registers
-      // the MMAs of this weight stage's previous use have finished reading it
-      got = g < kSA || mbar_wait(a_empty + sa, ((g / kSA) - 1) & 1);
+      // the MMAs of this stage's previous use have finished reading it
+      got = g < kS || mbar_wait(st_empty + s, ((g / kS) - 1) & 1);
       if (!__all_sync(0xffffffffu, got)) break;
       tc::tc_fence_after();
-      const uint32_t w[6] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y};
-      uint32_t pk[16];  // column e: K elements (2e, 2e+1) of the thread's 32
 #pragma unroll
-      for (int uu = 0; uu < 2; ++uu) {
-        const uint32_t w0 = w[3 * uu], w1 = w[3 * uu + 1], w2 = w[3 * uu + 2];
-        const uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
-                                w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
-                                w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
+      for (int h = 0; h < kG; ++h) {
+        uint32_t pk[16];  // column e: K elements (2e, 2e+1) of these 32
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          pk[8 * uu + e] = (__float_as_uint(code_to_float(f[2 * e])) >> 16) |
-                           (__float_as_uint(code_to_float(f[2 * e + 1])) & 0xFFFF0000u);
+        for (int uu = 0; uu < 2; ++uu) {
+          const uint32_t w0 = w[6 * h + 3 * uu], w1 = w[6 * h + 3 * uu + 1], w2 = w[6 * h + 3 * uu + 2];
+          const uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
+                                  w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
+                                  w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            pk[8 * uu + e] = (__float_as_uint(code_to_float(f[2 * e])) >> 16) |
+                             (__float_as_uint(code_to_float(f[2 * e + 1])) & 0xFFFF0000u);
+        }
+        tc::tmem_st16(a_lane + kAS * s + 16 * h, pk);
       }
-      tc::tmem_st16(a_lane + 32 * sa, pk);
       tc::tmem_wait_st();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(a_full + sa);
+      if (lane == 0) mbar_arrive(a_full + s);
     }
   }
 
