@@ -372,6 +372,138 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
   }
 }
 
+// Decode attention for one (sequence, kv head): the REP query heads of the
+// group share every K and V row load (attn_head_kernel reads each row once per
+// query head).  Per head, the scores, the maximum, the sum of exponentials and
+// the V accumulation keep attn_head_kernel's thread mapping and order, so the
+// outputs are bit-identical to it.
+template <int HD, int REP>
+__global__ void __launch_bounds__(256) attn_group_kernel(
+    const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+    int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
+    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int KV, int S, float denom,
+    const int32_t* __restrict__ seq) {
+  constexpr int CQ = HD / 4;  // float4 columns of a row
+  constexpr int G = 256 / CQ; // position groups in the V pass
+  extern __shared__ __align__(16) float sa[];
+  float* sq = sa;                                              // [REP][HD]
+  float* red = sq + REP * HD;                                  // [REP][16]
+  float4* part = reinterpret_cast<float4*>(red + REP * 16);    // [REP][G][CQ]
+  float* sp = reinterpret_cast<float*>(part + REP * G * CQ);   // [REP][S] scores, then exp
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.x, g = blockIdx.y;
+  float* o = out + (int64_t)b * ldo + g * REP * HD;
+  int T = len[b] + len_add;
+  T = T > S ? S : T;
+  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
+    for (int i = tid; i < REP * HD; i += 256) o[i] = 0.0f;
+    return;
+  }
+  const int kvr = KV * HD;
+  const int64_t crow = seq ? seq[b] : b;
+  const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + g * HD);
+  const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + g * HD);
+  for (int i = tid; i < REP * HD; i += 256) sq[i] = qb[(int64_t)b * ldq + g * REP * HD + i];
+  __syncthreads();
+  float mx[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) mx[r] = -INFINITY;
+  for (int t = tid; t < T; t += 256) {
+    const float4* kr = kb + (int64_t)t * (kvr / 4);
+    float d[REP];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) d[r] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CQ; ++j) {
+      const float4 k4 = __ldg(kr + j);
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const float4 q4 = reinterpret_cast<const float4*>(sq + r * HD)[j];
+        d[r] = fmaf(q4.x, k4.x, d[r]);
+        d[r] = fmaf(q4.y, k4.y, d[r]);
+        d[r] = fmaf(q4.z, k4.z, d[r]);
+        d[r] = fmaf(q4.w, k4.w, d[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float sc = __fdiv_rn(d[r], denom);
+      sp[r * S + t] = sc;
+      mx[r] = fmaxf(mx[r], sc);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], off));
+    if (lane == 0) red[r * 16 + warp] = mx[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float m = red[r * 16];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[r * 16 + w]);
+    mx[r] = m;
+  }
+  float sum[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) sum[r] = 0.0f;
+  for (int t = tid; t < T; t += 256) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float e = expf(sp[r * S + t] - mx[r]);
+      sp[r * S + t] = e;
+      sum[r] += e;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    sum[r] = warp_sum(sum[r]);
+    if (lane == 0) red[r * 16 + 8 + warp] = sum[r];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float sm = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sm += red[r * 16 + 8 + w];
+    sum[r] = sm;
+  }
+  const int cq = tid % CQ, grp = tid / CQ;
+  float4 acc[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = grp; t < T; t += G) {
+    const float4 v4 = __ldg(vb + (int64_t)t * (kvr / 4) + cq);
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float wt = __fdiv_rn(sp[r * S + t], sum[r]);
+      acc[r].x = fmaf(wt, v4.x, acc[r].x);
+      acc[r].y = fmaf(wt, v4.y, acc[r].y);
+      acc[r].z = fmaf(wt, v4.z, acc[r].z);
+      acc[r].w = fmaf(wt, v4.w, acc[r].w);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r) part[(r * G + grp) * CQ + cq] = acc[r];
+  __syncthreads();
+  for (int i = tid; i < REP * CQ; i += 256) {
+    const int r = i / CQ, c = i % CQ;
+    float4 x = part[r * G * CQ + c];
+    for (int k = 1; k < G; ++k) {
+      const float4 p = part[(r * G + k) * CQ + c];
+      x.x += p.x; x.y += p.y; x.z += p.z; x.w += p.w;
+    }
+    reinterpret_cast<float4*>(o + r * HD)[c] = x;
+  }
+}
+
+// Shared memory of attn_group_kernel for S positions.
+static size_t attn_group_smem(int hd, int rep, int S) {
+  return (size_t)rep * ((size_t)hd * 4 + 64 + 256 * 16 + (size_t)S * 4);
+}
+
 // Shared memory of attn_head_kernel for S positions.
 static size_t attn_head_smem(int hd, int S) { return (size_t)(hd + 16) * 4 + 256 * 16 + (size_t)S * 4; }
 
@@ -379,6 +511,20 @@ static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, cons
                              const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo, int S,
                              float denom, const int32_t* seq = nullptr) {
+  // many (sequence, kv head) pairs: one CTA per pair serves the group's query heads
+  const int rep = KV > 0 ? H / KV : 0;
+  if (n * KV >= 128 && KV * rep == H && KV <= 65535 && (rep == 2 || rep == 4 || rep == 8) &&
+      (hd == 64 || hd == 128) && attn_group_smem(hd, rep, S) <= 48 * 1024) {
+    const dim3 ggrid(n, KV);
+    const size_t gsm = attn_group_smem(hd, rep, S);
+#define Q6W_GROUP(HDV, REPV)                                                                                   \
+  if (hd == HDV && rep == REPV)                                                                                \
+    attn_group_kernel<HDV, REPV><<<ggrid, 256, gsm, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add,  \
+                                                         flags, out, ldo, KV, S, denom, seq);
+    Q6W_GROUP(64, 2) Q6W_GROUP(64, 4) Q6W_GROUP(64, 8) Q6W_GROUP(128, 2) Q6W_GROUP(128, 4) Q6W_GROUP(128, 8)
+#undef Q6W_GROUP
+    return true;
+  }
   const size_t smem = attn_head_smem(hd, S);
   if (smem > 48 * 1024 || H > 65535 || (hd != 64 && hd != 128)) return false;
   const dim3 grid(n, H);
