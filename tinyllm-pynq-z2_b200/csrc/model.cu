@@ -1142,8 +1142,7 @@ __global__ void prefill_argmax_kernel(int n, const unsigned long long* __restric
 // 64; wq|wk|wv, wo, w2 and vocab rows in whole 128-row tiles; W1/W3 in
 // 64-pair tiles.
 static bool tcg_shapes_ok(const q6w_model_desc& d, int kvr) {
-  if (d.dim > 8 * tcg::kImgThreads * tcg::kImgChunks || d.hidden_dim > 8 * tcg::kImgThreads * tcg::kImgChunks)
-    return false;
+  if (d.dim > tcg::kImgMaxK || d.hidden_dim > tcg::kImgMaxK) return false;
   // K (dim, hidden) in whole packed groups of kG x 64 columns
   return d.dim % (64 * tcg::kG) == 0 && d.hidden_dim % (64 * tcg::kG) == 0 && d.dim >= 256 && d.dim % 128 == 0 &&
          kvr % 128 == 0 && d.vocab_size % 128 == 0;
@@ -1278,7 +1277,7 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
 
 static int32_t tcg_image(const float* x, int ldx, int n, int K, const float* g, float eps, uint8_t* img,
                          cudaStream_t st) {
-  if (K % 8 || K > 8 * tcg::kImgThreads * tcg::kImgChunks) return fail(Q6W_ERR_ARG, "image of K=%d unsupported", K);
+  if (K % 16 || K > tcg::kImgMaxK) return fail(Q6W_ERR_ARG, "image of K=%d unsupported", K);
   tcg::image_kernel<<<n, tcg::kImgThreads, 0, st>>>(x, ldx, n, K, g, eps, img);
   Q6W_LAUNCH_CHECK("image_kernel");
   return Q6W_OK;

@@ -15,9 +15,10 @@
 //    by one 2-D TMA tensor load (no multicast; two 64-row boxes in GLU mode),
 //    6 steps deep;
 //  * expanded weights (3 stages of 64 columns) in tensor memory: the decode
-//    warps write the bf16 rows with tcgen05.st (row r on TMEM lane r, K
-//    elements 2e, 2e+1 in column e) and the MMA reads its A operand from
-//    there, so the expansion costs no shared-memory bandwidth;
+//    warps write the bf16 rows with tcgen05.st (row r on TMEM lane r, two K
+//    elements per column, in the pair order of expand_group) and the MMA
+//    reads its A operand from there, so the expansion costs no shared-memory
+//    bandwidth;
 //  * activations (3 stages of 48 KB): the 192 rows of both 64-column chunks,
 //    bulk-copied from the pre-swizzled activation image, the MMA's B operand.
 // One commit per step frees a weight stage and an activation stage together.
@@ -87,6 +88,38 @@ struct GArgs {
 struct GMaps {
   CUtensorMap m[3];
 };
+
+// ---- weight expansion -------------------------------------------------------
+// A 12-byte group (words w0, w1, w2) holds codes 0..15 at bits 6f.  Codes whose
+// bits start at the same offset inside their byte (0, 2, 4 or 6) are paired:
+// one byte permute puts the pair's bytes in the two 16-bit halves of a word,
+// one shift brings both codes to bits 0-5 and 16-21, one mask/xor makes each
+// half the bf16 of 128 + (c ^ 32) (the 7-bit mantissa holds it), and one bf16x2
+// subtraction of 160 leaves the signed value (c ^ 32) - 32 exactly.  The pairs, as TMEM columns
+// 0..7 of the group, hold codes (0,4) (8,12) (3,7) (11,15) (2,6) (10,14)
+// (1,5) (9,13): K order {0, 4, 8, 12, 3, 7, 11, 15, 2, 6, 10, 14, 1, 5, 9, 13}
+// inside each group, the order in which image_kernel writes the activations,
+// so the dot products are unchanged.
+__device__ __forceinline__ uint32_t code_pair_bf16(uint32_t t) {
+  // codes are two's complement: (c ^ 32) - 32 is the value (bit 5 flipped, as code_to_float)
+  const uint32_t u = (t & 0x003F003Fu) ^ 0x43204320u;  // bf16x2 (128 + (c0 ^ 32), 128 + (c1 ^ 32))
+  __nv_bfloat162_raw k;
+  k.x = 0x4320;  // 160
+  k.y = 0x4320;
+  const __nv_bfloat162 d = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u), __nv_bfloat162(k));
+  return *reinterpret_cast<const uint32_t*>(&d);
+}
+
+__device__ __forceinline__ void expand_group(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t* out) {
+  out[0] = code_pair_bf16(__byte_perm(w0, 0u, 0x3300));        // codes 0, 4   (offset 0)
+  out[1] = code_pair_bf16(__byte_perm(w1, w2, 0x5522));        // codes 8, 12  (offset 0)
+  out[2] = code_pair_bf16(__byte_perm(w0, w1, 0x5522) >> 2);   // codes 3, 7   (offset 2)
+  out[3] = code_pair_bf16(__byte_perm(w2, 0u, 0x3300) >> 2);   // codes 11, 15 (offset 2)
+  out[4] = code_pair_bf16(__byte_perm(w0, w1, 0x5421) >> 4);   // codes 2, 6   (offset 4)
+  out[5] = code_pair_bf16(__byte_perm(w1, w2, 0x7643) >> 4);   // codes 10, 14 (offset 4)
+  out[6] = code_pair_bf16(__byte_perm(w0, w1, 0x4310) >> 6);   // codes 1, 5   (offset 6)
+  out[7] = code_pair_bf16(__byte_perm(w1, w2, 0x6532) >> 6);   // codes 9, 13  (offset 6)
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -286,18 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       tc::tc_fence_after();
 #pragma unroll
       for (int h = 0; h < kG; ++h) {
-        uint32_t pk[16];  // column e: K elements (2e, 2e+1) of these 32
+        uint32_t pk[16];  // two 16-column groups in expand_group's K order
 #pragma unroll
-        for (int uu = 0; uu < 2; ++uu) {
-          const uint32_t w0 = w[6 * h + 3 * uu], w1 = w[6 * h + 3 * uu + 1], w2 = w[6 * h + 3 * uu + 2];
-          const uint32_t f[16] = {w0, w0 >> 6, w0 >> 12, w0 >> 18, w0 >> 24, __funnelshift_r(w0, w1, 30),
-                                  w1 >> 4, w1 >> 10, w1 >> 16, w1 >> 22, __funnelshift_r(w1, w2, 28),
-                                  w2 >> 2, w2 >> 8, w2 >> 14, w2 >> 20, w2 >> 26};
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            pk[8 * uu + e] = (__float_as_uint(code_to_float(f[2 * e])) >> 16) |
-                             (__float_as_uint(code_to_float(f[2 * e + 1])) & 0xFFFF0000u);
-        }
+        for (int uu = 0; uu < 2; ++uu) expand_group(w[6 * h + 3 * uu], w[6 * h + 3 * uu + 1], w[6 * h + 3 * uu + 2], pk + 8 * uu);
         tc::tmem_st16(a_lane + kAS * s + 16 * h, pk);
       }
       tc::tmem_wait_st();
@@ -432,11 +456,14 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
 
 // Activation image (tc.cuh layout, K columns) of rows x[0..n): RMSNorm with
 // weight g when g is given (torch_benchmark.py:22-24), else the rows as they
-// are.  One CTA of 256 threads per row, each thread 8-column chunks
-// k0 = 8 tid + 2048 i (K <= 6144: at most three per thread), all loaded before
-// the reduction; rows beyond n are left as they are (never used).
+// are.  Inside every 16-column group the columns are stored in the order the
+// weight expansion produces them (expand_group): image position p of a group
+// holds column {0, 4, 8, 12, 3, 7, 11, 15, 2, 6, 10, 14, 1, 5, 9, 13}[p].  One CTA of 256 threads per row, each thread 16-column
+// groups 16 (tid + 256 i) (K <= 8192: at most two per thread), all loaded
+// before the reduction; rows beyond n are left as they are (never used).
 constexpr int kImgThreads = 256;
-constexpr int kImgChunks = 3;
+constexpr int kImgGroups = 2;
+constexpr int kImgMaxK = 16 * kImgThreads * kImgGroups;
 
 __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restrict__ x, int ldx, int n, int K,
                                                             const float* __restrict__ g, float eps,
@@ -446,24 +473,25 @@ __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restr
   const int64_t row = blockIdx.x;
   if (row >= n) return;
   const float* xr = x + row * ldx;
-  float v[kImgChunks][8];
+  float v[kImgGroups][16];
 #pragma unroll
-  for (int c = 0; c < kImgChunks; ++c) {
-    const int k0 = 8 * tid + 8 * kImgThreads * c;
+  for (int c = 0; c < kImgGroups; ++c) {
+    const int k0 = 16 * (tid + kImgThreads * c);
     if (k0 < K) {
-      const float4 lo = *reinterpret_cast<const float4*>(xr + k0);
-      const float4 hi = *reinterpret_cast<const float4*>(xr + k0 + 4);
-      v[c][0] = lo.x; v[c][1] = lo.y; v[c][2] = lo.z; v[c][3] = lo.w;
-      v[c][4] = hi.x; v[c][5] = hi.y; v[c][6] = hi.z; v[c][7] = hi.w;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 f = *reinterpret_cast<const float4*>(xr + k0 + 4 * q);
+        v[c][4 * q] = f.x; v[c][4 * q + 1] = f.y; v[c][4 * q + 2] = f.z; v[c][4 * q + 3] = f.w;
+      }
     }
   }
   if (g) {
     float ss = 0.0f;
 #pragma unroll
-    for (int c = 0; c < kImgChunks; ++c)
-      if (8 * tid + 8 * kImgThreads * c < K)
+    for (int c = 0; c < kImgGroups; ++c)
+      if (16 * (tid + kImgThreads * c) < K)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[c][i], v[c][i]));
+        for (int i = 0; i < 16; ++i) ss = __fadd_rn(ss, __fmul_rn(v[c][i], v[c][i]));
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
@@ -471,17 +499,22 @@ __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restr
     t = warp_sum(t);
     const float r = rms_scale(t, K, eps);
 #pragma unroll
-    for (int c = 0; c < kImgChunks; ++c) {
-      const int k0 = 8 * tid + 8 * kImgThreads * c;
+    for (int c = 0; c < kImgGroups; ++c) {
+      const int k0 = 16 * (tid + kImgThreads * c);
       if (k0 < K)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[c][i] = __fmul_rn(__fmul_rn(v[c][i], r), __ldg(g + k0 + i));
+        for (int i = 0; i < 16; ++i) v[c][i] = __fmul_rn(__fmul_rn(v[c][i], r), __ldg(g + k0 + i));
     }
   }
 #pragma unroll
-  for (int c = 0; c < kImgChunks; ++c) {
-    const int k0 = 8 * tid + 8 * kImgThreads * c;
-    if (k0 < K) tc::img_store8(img, row, k0, K, v[c]);
+  for (int c = 0; c < kImgGroups; ++c) {
+    const int k0 = 16 * (tid + kImgThreads * c);
+    if (k0 < K) {
+      const float lo[8] = {v[c][0], v[c][4], v[c][8], v[c][12], v[c][3], v[c][7], v[c][11], v[c][15]};
+      const float hi[8] = {v[c][2], v[c][6], v[c][10], v[c][14], v[c][1], v[c][5], v[c][9], v[c][13]};
+      tc::img_store8(img, row, k0, K, lo);
+      tc::img_store8(img, row, k0 + 8, K, hi);
+    }
   }
 }
 
