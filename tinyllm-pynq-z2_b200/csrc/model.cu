@@ -20,6 +20,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -377,7 +378,9 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
 // query head).  Per head, the scores, the maximum, the sum of exponentials and
 // the V accumulation keep attn_head_kernel's thread mapping and order, so the
 // outputs are bit-identical to it.
-template <int HD, int REP>
+// STAGE_V: the group's V rows [0, T) are copied into shared memory (cp.async)
+// at the start, so their latency hides behind the score phase.
+template <int HD, int REP, bool STAGE_V>
 __global__ void __launch_bounds__(256) attn_group_kernel(
     const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
@@ -390,6 +393,7 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
   float* red = sq + REP * HD;                                  // [REP][16]
   float4* part = reinterpret_cast<float4*>(red + REP * 16);    // [REP][G][CQ]
   float* sp = reinterpret_cast<float*>(part + REP * G * CQ);   // [REP][S] scores, then exp
+  float4* sv = reinterpret_cast<float4*>(sp + ((REP * S + 3) & ~3));  // STAGE_V: [S][CQ] V rows, 16-B aligned
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.x, g = blockIdx.y;
   float* o = out + (int64_t)b * ldo + g * REP * HD;
@@ -403,6 +407,15 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
   const int64_t crow = seq ? seq[b] : b;
   const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + g * HD);
   const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + g * HD);
+  if (STAGE_V) {
+    for (int i = tid; i < T * CQ; i += 256) {
+      const int t = i / CQ, c = i % CQ;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sv + i)),
+                   "l"(vb + (int64_t)t * (kvr / 4) + c)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   for (int i = tid; i < REP * HD; i += 256) sq[i] = qb[(int64_t)b * ldq + g * REP * HD + i];
   __syncthreads();
   float mx[REP];
@@ -462,6 +475,7 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
     sum[r] = warp_sum(sum[r]);
     if (lane == 0) red[r * 16 + 8 + warp] = sum[r];
   }
+  if (STAGE_V) asm volatile("cp.async.wait_group 0;" ::: "memory");  // this thread's V copies landed
   __syncthreads();
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
@@ -475,7 +489,7 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
 #pragma unroll
   for (int r = 0; r < REP; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = grp; t < T; t += G) {
-    const float4 v4 = __ldg(vb + (int64_t)t * (kvr / 4) + cq);
+    const float4 v4 = STAGE_V ? sv[t * CQ + cq] : __ldg(vb + (int64_t)t * (kvr / 4) + cq);
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       const float wt = __fdiv_rn(sp[r * S + t], sum[r]);
@@ -499,9 +513,29 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
   }
 }
 
-// Shared memory of attn_group_kernel for S positions.
-static size_t attn_group_smem(int hd, int rep, int S) {
-  return (size_t)rep * ((size_t)hd * 4 + 64 + 256 * 16 + (size_t)S * 4);
+// Shared memory of attn_group_kernel for S positions (+ the staged V rows).
+static size_t attn_group_smem(int hd, int rep, int S, bool stage_v) {
+  return (size_t)rep * ((size_t)hd * 4 + 64 + 256 * 16 + (size_t)S * 4) + (stage_v ? (size_t)S * hd * 4 + 16 : 0);
+}
+
+// The V-staging kernels need more than the default 48 KB of dynamic shared
+// memory: allowed once per process (model creation and the attention op call
+// this before any launch); two CTAs still fit on an SM.
+constexpr size_t kAttnStageMax = 110 * 1024;
+static bool g_attn_stage_ok = false;
+static void attn_group_setup() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    bool ok = true;
+#define Q6W_GROUP_ATTR(HDV, REPV)                                                                          \
+  ok = ok && cudaFuncSetAttribute(attn_group_kernel<HDV, REPV, true>,                                      \
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnStageMax) == cudaSuccess;
+    Q6W_GROUP_ATTR(64, 2) Q6W_GROUP_ATTR(64, 4) Q6W_GROUP_ATTR(64, 8)
+    Q6W_GROUP_ATTR(128, 2) Q6W_GROUP_ATTR(128, 4) Q6W_GROUP_ATTR(128, 8)
+#undef Q6W_GROUP_ATTR
+    if (!ok) cudaGetLastError();
+    g_attn_stage_ok = ok;
+  });
 }
 
 // Shared memory of attn_head_kernel for S positions.
@@ -513,14 +547,20 @@ static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, cons
                              float denom, const int32_t* seq = nullptr) {
   // many (sequence, kv head) pairs: one CTA per pair serves the group's query heads
   const int rep = KV > 0 ? H / KV : 0;
+  const bool stage = g_attn_stage_ok && attn_group_smem(hd, rep, S, true) <= kAttnStageMax;
   if (n * KV >= 128 && KV * rep == H && KV <= 65535 && (rep == 2 || rep == 4 || rep == 8) &&
-      (hd == 64 || hd == 128) && attn_group_smem(hd, rep, S) <= 48 * 1024) {
+      (hd == 64 || hd == 128) && (stage || attn_group_smem(hd, rep, S, false) <= 48 * 1024)) {
     const dim3 ggrid(n, KV);
-    const size_t gsm = attn_group_smem(hd, rep, S);
-#define Q6W_GROUP(HDV, REPV)                                                                                   \
-  if (hd == HDV && rep == REPV)                                                                                \
-    attn_group_kernel<HDV, REPV><<<ggrid, 256, gsm, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add,  \
-                                                         flags, out, ldo, KV, S, denom, seq);
+    const size_t gsm = attn_group_smem(hd, rep, S, stage);
+#define Q6W_GROUP(HDV, REPV)                                                                                    \
+  if (hd == HDV && rep == REPV) {                                                                               \
+    if (stage)                                                                                                  \
+      attn_group_kernel<HDV, REPV, true><<<ggrid, 256, gsm, st>>>(qb, ldq, kc, vc, cstride, layer_off, len,     \
+                                                                  len_add, flags, out, ldo, KV, S, denom, seq); \
+    else                                                                                                        \
+      attn_group_kernel<HDV, REPV, false><<<ggrid, 256, gsm, st>>>(qb, ldq, kc, vc, cstride, layer_off, len,    \
+                                                                   len_add, flags, out, ldo, KV, S, denom, seq); \
+  }
     Q6W_GROUP(64, 2) Q6W_GROUP(64, 4) Q6W_GROUP(64, 8) Q6W_GROUP(128, 2) Q6W_GROUP(128, 4) Q6W_GROUP(128, 8)
 #undef Q6W_GROUP
     return true;
@@ -1528,6 +1568,11 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
     }
     const char* offg = getenv("Q6W_DISABLE_TCG");
     M->use_tcg = !M->use_tc && !(offg && offg[0] == '1') && major == 10 && tcg_shapes_ok(d, kvr);
+    // the image kernel reads the norm weights as float4
+    for (int l = 0; l < d.n_layers && M->use_tcg; ++l)
+      M->use_tcg = aligned(M->layers[l].attention_norm, 16) && aligned(M->layers[l].ffn_norm, 16);
+    M->use_tcg = M->use_tcg && aligned(d.norm, 16);
+    attn_group_setup();
     if (M->use_tcg && tcg_set_attrs() != cudaSuccess) {
       cudaGetLastError();
       M->use_tcg = false;  // the SIMT kernels still serve every shape
@@ -1919,6 +1964,7 @@ extern "C" int32_t q6w_gqa_attention(const float* queries, const float* keys, co
     Q6W_LAUNCH_CHECK("attn_rows_kernel");
     return Q6W_OK;
   }
+  attn_group_setup();
   if (launch_attn_head(head_dim, n, H, kv_heads, s, queries, ld, keys, values, kv_seq_stride, 0, lengths, 0, nullptr,
                        output, ld, max_len, denom)) {
     Q6W_LAUNCH_CHECK("attn_head_kernel");

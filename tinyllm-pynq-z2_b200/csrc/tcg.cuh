@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restr
   const int64_t row = blockIdx.x;
   if (row >= n) return;
   const float* xr = x + row * ldx;
-  float v[kImgGroups][16];
+  float v[kImgGroups][16], gw[kImgGroups][16];  // the norm weights load with x, before the reduction
 #pragma unroll
   for (int c = 0; c < kImgGroups; ++c) {
     const int k0 = 16 * (tid + kImgThreads * c);
@@ -482,6 +482,8 @@ __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restr
       for (int q = 0; q < 4; ++q) {
         const float4 f = *reinterpret_cast<const float4*>(xr + k0 + 4 * q);
         v[c][4 * q] = f.x; v[c][4 * q + 1] = f.y; v[c][4 * q + 2] = f.z; v[c][4 * q + 3] = f.w;
+        const float4 w = g ? __ldg(reinterpret_cast<const float4*>(g + k0 + 4 * q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        gw[c][4 * q] = w.x; gw[c][4 * q + 1] = w.y; gw[c][4 * q + 2] = w.z; gw[c][4 * q + 3] = w.w;
       }
     }
   }
@@ -503,7 +505,7 @@ __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restr
       const int k0 = 16 * (tid + kImgThreads * c);
       if (k0 < K)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[c][i] = __fmul_rn(__fmul_rn(v[c][i], r), __ldg(g + k0 + i));
+        for (int i = 0; i < 16; ++i) v[c][i] = __fmul_rn(__fmul_rn(v[c][i], r), gw[c][i]);
     }
   }
 #pragma unroll
