@@ -49,10 +49,10 @@ struct LinearLauncher {
     return true;
   }
 
-  template <int WC>
+  template <int WC, int MINB>
   static cudaError_t stream_launch_wc(const float* x, const float* g, float eps, const MatSet& ms,
                                       const EpiArgs& ep, const stream::Geometry& geo, cudaStream_t st) {
-    auto kern = stream::stream_gemv_kernel<RMS, EPI, WC>;
+    auto kern = stream::stream_gemv_kernel<RMS, EPI, WC, MINB>;
     static bool configured = false;  // per instantiation: the size is a compile-time constant
     if (!configured) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)geo.smem);
@@ -60,7 +60,8 @@ struct LinearLauncher {
       configured = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min(geo.tiles, 2 * sm_count()));  // two CTAs per SM
+    // two CTAs per SM, three for large matrices (K <= 2048 there: the stages of three fit)
+    cfg.gridDim = dim3((unsigned)std::min(geo.tiles, (MINB == 3 ? 3 : 2) * sm_count()));
     cfg.blockDim = dim3((unsigned)geo.threads);
     cfg.dynamicSmemBytes = geo.smem;
     cfg.stream = st;
@@ -74,12 +75,15 @@ struct LinearLauncher {
 
   static cudaError_t stream_launch(const float* x, const float* g, float eps, const MatSet& ms, const EpiArgs& ep,
                                    const stream::Geometry& geo, cudaStream_t st) {
+    const bool big = geo.tiles >= 3 * sm_count();
     switch (geo.wc) {
-      case 1: return stream_launch_wc<1>(x, g, eps, ms, ep, geo, st);
-      case 2: return stream_launch_wc<2>(x, g, eps, ms, ep, geo, st);
-      case 4: return stream_launch_wc<4>(x, g, eps, ms, ep, geo, st);
-      case 8: return stream_launch_wc<8>(x, g, eps, ms, ep, geo, st);
-      default: return stream_launch_wc<11>(x, g, eps, ms, ep, geo, st);
+      case 1: return stream_launch_wc<1, 1>(x, g, eps, ms, ep, geo, st);
+      case 2: return big ? stream_launch_wc<2, 3>(x, g, eps, ms, ep, geo, st)
+                         : stream_launch_wc<2, 1>(x, g, eps, ms, ep, geo, st);
+      case 4: return big ? stream_launch_wc<4, 3>(x, g, eps, ms, ep, geo, st)
+                         : stream_launch_wc<4, 1>(x, g, eps, ms, ep, geo, st);
+      case 8: return stream_launch_wc<8, 1>(x, g, eps, ms, ep, geo, st);
+      default: return stream_launch_wc<11, 1>(x, g, eps, ms, ep, geo, st);
     }
   }
 
