@@ -264,7 +264,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   __shared__ uint64_t mma_bar, ld_bar;
   __shared__ uint32_t tmem_base;
   __shared__ __align__(16) float sscale[256];
-  __shared__ float ss_part[2][kM];
   __shared__ int timed_out;
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -477,48 +476,71 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
-    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim; this thread: columns 64*half..+63
-      float xn[64];
-      float ss = 0.0f;
+    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim
+      // Two passes through shared memory (sB: the weights are consumed once the
+      // MMAs are done), so every global access is row-contiguous.
+      // E1: this thread's row (TMEM lane) and columns 64*half..+63, scaled,
+      // into sB as float4 unit c4 of row r at r*32 + (c4 ^ (r & 7)).
+      float4* st4 = reinterpret_cast<float4*>(sB);
 #pragma unroll
       for (int cc = 0; cc < 64; cc += 32) {
         const int c0 = half * 64 + cc;
         float v[32];
         tmem_ld32(lane_addr + c0, v);
-        if (live) {
-          const float4* xr = reinterpret_cast<const float4*>(a.x + m * 128 + c0);
-          const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
+        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 o = xr[i];
-            const float4 sc = s4[i];
-            xn[cc + 4 * i] = __fadd_rn(o.x, __fmul_rn(v[4 * i], sc.x));
-            xn[cc + 4 * i + 1] = __fadd_rn(o.y, __fmul_rn(v[4 * i + 1], sc.y));
-            xn[cc + 4 * i + 2] = __fadd_rn(o.z, __fmul_rn(v[4 * i + 2], sc.z));
-            xn[cc + 4 * i + 3] = __fadd_rn(o.w, __fmul_rn(v[4 * i + 3], sc.w));
-          }
+        for (int i = 0; i < 8; ++i) {
+          const float4 sc = s4[i];
+          st4[row * 32 + (((c0 >> 2) + i) ^ (row & 7))] =
+              make_float4(__fmul_rn(v[4 * i], sc.x), __fmul_rn(v[4 * i + 1], sc.y), __fmul_rn(v[4 * i + 2], sc.z),
+                          __fmul_rn(v[4 * i + 3], sc.w));
         }
       }
-      if (live) {
-        float4* xw = reinterpret_cast<float4*>(a.x + m * 128 + half * 64);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          xw[i] = make_float4(xn[4 * i], xn[4 * i + 1], xn[4 * i + 2], xn[4 * i + 3]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(xn[4 * i + e], xn[4 * i + e]));
-        }
-      }
-      ss_part[half][row] = ss;
       __syncthreads();
-      if (live) {
-        const float rstd = rms_scale(__fadd_rn(ss_part[0][row], ss_part[1][row]), 128, a.eps);
+      // E2: half-warps take rows (16 lanes x 8 columns = one row): residual add,
+      // x written back, the row's sum of squares over the 16 lanes, RMSNorm with
+      // the next norm weight, and the row's image units.
+      const int lane = tid & 31, sub = lane >> 4, cb = 8 * (lane & 15);
+      float gw[8];
 #pragma unroll
-        for (int k0 = 0; k0 < 64; k0 += 8) {
+      for (int i = 0; i < 8; ++i) gw[i] = __ldg(a.gnorm + cb + i);
+      // the residual rows of all eight passes are loaded first, so the loads overlap
+      float4 ox[kM / 16][2];
+#pragma unroll
+      for (int i = 0; i < kM / 16; ++i) {
+        const int64_t mr = (int64_t)mt * kM + 2 * (warp + 8 * i) + sub;
+        const float4* xr = reinterpret_cast<const float4*>(a.x + mr * 128 + cb);
+        ox[i][0] = mr < a.n ? xr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ox[i][1] = mr < a.n ? xr[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kM / 16; ++i) {
+        const int r = 2 * (warp + 8 * i) + sub;
+        const int64_t mr = (int64_t)mt * kM + r;
+        const bool lv = mr < a.n;  // uniform over the 16 lanes of the row
+        const float4 p0 = st4[r * 32 + ((cb >> 2) ^ (r & 7))], p1 = st4[r * 32 + (((cb >> 2) + 1) ^ (r & 7))];
+        float xn[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (lv) {
+          float4* xr = reinterpret_cast<float4*>(a.x + mr * 128 + cb);
+          const float4 o0 = ox[i][0], o1 = ox[i][1];
+          xn[0] = __fadd_rn(o0.x, p0.x); xn[1] = __fadd_rn(o0.y, p0.y);
+          xn[2] = __fadd_rn(o0.z, p0.z); xn[3] = __fadd_rn(o0.w, p0.w);
+          xn[4] = __fadd_rn(o1.x, p1.x); xn[5] = __fadd_rn(o1.y, p1.y);
+          xn[6] = __fadd_rn(o1.z, p1.z); xn[7] = __fadd_rn(o1.w, p1.w);
+          xr[0] = make_float4(xn[0], xn[1], xn[2], xn[3]);
+          xr[1] = make_float4(xn[4], xn[5], xn[6], xn[7]);
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(xn[e], xn[e]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if (lv) {
+          const float rstd = rms_scale(ss, 128, a.eps);
           float u8[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            u8[i] = __fmul_rn(__fmul_rn(xn[k0 + i], rstd), __ldg(a.gnorm + half * 64 + k0 + i));
-          img_store8(a.out_img, m, half * 64 + k0, 128, u8);
+          for (int e = 0; e < 8; ++e) u8[e] = __fmul_rn(__fmul_rn(xn[e], rstd), gw[e]);
+          img_store8(a.out_img, mr, cb, 128, u8);
         }
       }
     } else if (EPI == TEPI_GLU) {  // N == 256: columns j (W1) and 128 + j (W3); this thread: j in 64*half..
