@@ -265,6 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   __shared__ uint32_t tmem_base;
   __shared__ __align__(16) float sscale[256];
   __shared__ int timed_out;
+  __shared__ int s_ok[kM], s_pos[kM];  // QKV epilogue: per row
+  __shared__ int64_t s_crow[kM];
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;                       // [3][2][128][128 B] = 96 KB (one K stage)
@@ -422,9 +424,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
       }
       if (live && bi >= 0) atomicMax(ep.keys + m, argmax_key(bv, bi));
     } else if (EPI == TEPI_QKV) {
+      // Columns in two blocks through shared memory (sB): block 0 the q rows
+      // [0, 128), block 1 the k and v rows [128, N).  E1 (this thread's row):
+      // scale and RoPE, into sB unit c4 of row r at r*32 + (c4 ^ (r & 7));
+      // E2: lanes of a row store contiguous runs of q, k and v.
       const EpiArgs& ep = a.ep;
       const bool ok = live && !(ep.flags[m] & SEQ_INVALID);
       const int pos = ok ? ep.pos[m] : 0;
+      s_ok[row] = ok;
+      s_pos[row] = pos;
+      s_crow[row] = ok && ep.seq ? ep.seq[m] : m;
       const int hh = ep.hd >> 1;  // 8 or 16 rotation frequencies
       float cs[16], sn[16];
       if (ok) {
@@ -434,47 +443,66 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
           sn[i] = i < hh ? __ldg(ep.rope_sin + (int64_t)pos * hh + i) : 0.0f;
         }
       }
-      const int cb = half * (a.N >> 1), ce = cb + (a.N >> 1);
-      for (int c0 = cb; c0 < ce; c0 += 32) {
-        float v[32];
-        tmem_ld32(lane_addr + c0, v);
-        if (!ok) continue;
-        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
+      float4* st4 = reinterpret_cast<float4*>(sB);
+      const int lane = tid & 31;
+#pragma unroll 1
+      for (int b = 0; b < 2; ++b) {
+        const int bw = b == 0 ? 128 : a.N - 128;  // block width: 128, or 2 kv_rows (64 or 128)
+        const int hw = bw >> 1;
+        for (int cc = 0; cc < hw; cc += 32) {
+          const int lc = half * hw + cc;  // column in the block
+          const int c0 = 128 * b + lc;    // column of the tile
+          float v[32];
+          tmem_ld32(lane_addr + c0, v);
+          const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 sc = s4[i];
-          v[4 * i] = __fmul_rn(v[4 * i], sc.x);
-          v[4 * i + 1] = __fmul_rn(v[4 * i + 1], sc.y);
-          v[4 * i + 2] = __fmul_rn(v[4 * i + 2], sc.z);
-          v[4 * i + 3] = __fmul_rn(v[4 * i + 3], sc.w);
-        }
-        const int v0 = nt * a.N + c0;  // first virtual row of this chunk
-        if (v0 < ep.q_rows + ep.kv_rows) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int j = ((v0 + i) & (ep.hd - 1)) >> 1;
-            float c = cs[0], sv = sn[0];
-#pragma unroll
-            for (int f = 1; f < 16; ++f)
-              if (f == j) { c = cs[f]; sv = sn[f]; }
-            const float ra = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + 1], sv));
-            const float rb = __fadd_rn(__fmul_rn(v[i], sv), __fmul_rn(v[i + 1], c));
-            v[i] = ra;
-            v[i + 1] = rb;
+          for (int i = 0; i < 8; ++i) {
+            const float4 sc = s4[i];
+            v[4 * i] = __fmul_rn(v[4 * i], sc.x);
+            v[4 * i + 1] = __fmul_rn(v[4 * i + 1], sc.y);
+            v[4 * i + 2] = __fmul_rn(v[4 * i + 2], sc.z);
+            v[4 * i + 3] = __fmul_rn(v[4 * i + 3], sc.w);
           }
-        }
-        float* dst;
-        const int64_t crow = ep.seq ? ep.seq[m] : m;
-        if (v0 < ep.q_rows)
-          dst = ep.qbuf + m * ep.ldq + v0;
-        else if (v0 < ep.q_rows + ep.kv_rows)
-          dst = ep.kc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v0 - ep.q_rows);
-        else
-          dst = ep.vc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
-                (v0 - ep.q_rows - ep.kv_rows);
-        float4* d4 = reinterpret_cast<float4*>(dst);
+          const int v0 = nt * a.N + c0;  // first virtual row of this chunk
+          if (ok && v0 < ep.q_rows + ep.kv_rows) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            for (int i = 0; i < 32; i += 2) {
+              const int j = ((v0 + i) & (ep.hd - 1)) >> 1;
+              float c = cs[0], sv = sn[0];
+#pragma unroll
+              for (int f = 1; f < 16; ++f)
+                if (f == j) { c = cs[f]; sv = sn[f]; }
+              const float ra = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + 1], sv));
+              const float rb = __fadd_rn(__fmul_rn(v[i], sv), __fmul_rn(v[i + 1], c));
+              v[i] = ra;
+              v[i + 1] = rb;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            st4[row * 32 + (((lc >> 2) + i) ^ (row & 7))] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+        __syncthreads();
+        const int lpr = bw >> 3;  // lanes per row, 8 columns each
+        const int rpi = 32 / lpr, sub = lane / lpr, cb = 8 * (lane % lpr);
+        for (int r0 = 16 * warp; r0 < 16 * warp + 16; r0 += rpi) {
+          const int r = r0 + sub;
+          if (!s_ok[r]) continue;
+          const int64_t mr = (int64_t)mt * kM + r;
+          const float4 p0 = st4[r * 32 + ((cb >> 2) ^ (r & 7))], p1 = st4[r * 32 + (((cb >> 2) + 1) ^ (r & 7))];
+          const int v0 = nt * a.N + 128 * b + cb;
+          float* dst;
+          if (v0 < ep.q_rows)
+            dst = ep.qbuf + mr * ep.ldq + v0;
+          else if (v0 < ep.q_rows + ep.kv_rows)
+            dst = ep.kc + s_crow[r] * ep.cache_stride + ep.layer_off + (int64_t)s_pos[r] * ep.kv_rows + (v0 - ep.q_rows);
+          else
+            dst = ep.vc + s_crow[r] * ep.cache_stride + ep.layer_off + (int64_t)s_pos[r] * ep.kv_rows +
+                  (v0 - ep.q_rows - ep.kv_rows);
+          reinterpret_cast<float4*>(dst)[0] = p0;
+          reinterpret_cast<float4*>(dst)[1] = p1;
+        }
+        __syncthreads();  // the next block reuses sB
       }
     } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim
       // Two passes through shared memory (sB: the weights are consumed once the
