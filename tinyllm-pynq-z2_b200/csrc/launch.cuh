@@ -75,7 +75,8 @@ struct LinearLauncher {
 
   static cudaError_t stream_launch(const float* x, const float* g, float eps, const MatSet& ms, const EpiArgs& ep,
                                    const stream::Geometry& geo, cudaStream_t st) {
-    const bool big = geo.tiles >= 3 * sm_count();
+    // with the RMSNorm prologue every CTA normalises the row again: more CTAs cost more than they hide
+    const bool big = !RMS && geo.tiles >= 3 * sm_count();
     switch (geo.wc) {
       case 1: return stream_launch_wc<1, 1>(x, g, eps, ms, ep, geo, st);
       case 2: return big ? stream_launch_wc<2, 3>(x, g, eps, ms, ep, geo, st)

@@ -169,8 +169,9 @@ inline bool geometry(const MatSet& ms, Geometry& g) {
 }
 
 // MINB: CTAs per SM the register allocation leaves room for (3 for matrices
-// with at least three tiles per SM: more warps hide the shared-memory latency
-// of the decode; 1 otherwise, where the grid has at most two CTAs per SM).
+// with at least three tiles per SM and no RMSNorm prologue: more warps hide
+// the shared-memory latency of the decode; 1 otherwise, where the grid has at
+// most two CTAs per SM).
 template <bool RMS, int EPI, int WC, int MINB = 1>
 __global__ void __launch_bounds__(Shape<WC>::kThreads, MINB)
     stream_gemv_kernel(const float* __restrict__ x, const float* __restrict__ gnorm, float eps, MatSet ms,
