@@ -1014,8 +1014,10 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.q0 = L.wq.packed; a.q1 = L.wk.packed; a.q2 = L.wv.packed;
       a.s0 = L.wq.scales; a.s1 = L.wk.scales; a.s2 = L.wv.scales;
       a.end0 = dim; a.end1 = dim + kvr;
-      a.N = dim + 2 * kvr;
-      a.n_tiles = 1;
+      // two tiles of 128 rows (q | k v) give twice the CTAs when the rows divide
+      const int qkv_rows = dim + 2 * kvr;
+      a.N = qkv_rows % 128 == 0 ? 128 : qkv_rows;
+      a.n_tiles = qkv_rows / a.N;
       a.ep.qbuf = w.qb; a.ep.ldq = dim;
       a.ep.kc = kc; a.ep.vc = vc; a.ep.cache_stride = cstride; a.ep.layer_off = layer_off;
       a.ep.rope_cos = d.rope_cos; a.ep.rope_sin = d.rope_sin;

@@ -219,10 +219,18 @@ __device__ __forceinline__ int b_segments(const TcArgs& a, int epi, int nt, Seg 
     return 2;
   }
   if (epi == TEPI_QKV) {
-    sg[0] = {a.q0, a.s0, 0, a.end0};
-    sg[1] = {a.q1, a.s1, 0, a.end1 - a.end0};
-    sg[2] = {a.q2, a.s2, 0, a.N - a.end1};
-    return 3;
+    // rows [nt N, nt N + N) of the concatenation wq | wk | wv (end0, end1: its
+    // matrix boundaries; the last matrix ends at n_tiles N)
+    const int v0 = nt * a.N, v1 = v0 + a.N;
+    const int lo[3] = {0, a.end0, a.end1}, hi[3] = {a.end0, a.end1, a.n_tiles * a.N};
+    const uint8_t* qs[3] = {a.q0, a.q1, a.q2};
+    const float* ss[3] = {a.s0, a.s1, a.s2};
+    int k = 0;
+    for (int i = 0; i < 3; ++i) {
+      const int b0 = v0 > lo[i] ? v0 : lo[i], b1 = v1 < hi[i] ? v1 : hi[i];
+      if (b1 > b0) sg[k++] = {qs[i], ss[i], b0 - lo[i], b1 - b0};
+    }
+    return k;
   }
   sg[0] = {a.q0, a.s0, nt * a.N, a.N};
   return 1;
@@ -447,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
       const int lane = tid & 31;
 #pragma unroll 1
       for (int b = 0; b < 2; ++b) {
-        const int bw = b == 0 ? 128 : a.N - 128;  // block width: 128, or 2 kv_rows (64 or 128)
+        const int bw = b == 0 ? (a.N < 128 ? a.N : 128) : a.N - 128;  // block width (a multiple of 64)
+        if (bw <= 0) break;  // a tile of 128 rows has one block
         const int hw = bw >> 1;
         for (int cc = 0; cc < hw; cc += 32) {
           const int lc = half * hw + cc;  // column in the block
