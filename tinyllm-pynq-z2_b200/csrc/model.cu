@@ -1044,8 +1044,10 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.a_img = w.xs_img;
       a.K = dim;
       a.q0 = L.w1.packed; a.s0 = L.w1.scales; a.q1 = L.w3.packed; a.s1 = L.w3.scales;
-      a.N = 256;
-      a.n_tiles = hid / 128;
+      // tiles of 64 W1 + 64 W3 rows: more, smaller items spread over the SMs
+      // (each CTA keeps its activation tile across consecutive items)
+      a.N = 128;
+      a.n_tiles = hid / 64;
       a.out_img = w.hs_img; a.out_K = hid;
       if ((rc = tc_launch(tc::TEPI_GLU, a, M->sm_count, st))) return rc;
     }

@@ -213,9 +213,9 @@ struct Seg {
 };
 
 __device__ __forceinline__ int b_segments(const TcArgs& a, int epi, int nt, Seg (&sg)[3]) {
-  if (epi == TEPI_GLU) {
-    sg[0] = {a.q0, a.s0, nt * 128, 128};
-    sg[1] = {a.q1, a.s1, nt * 128, 128};
+  if (epi == TEPI_GLU) {  // N / 2 rows of W1, then the same rows of W3
+    sg[0] = {a.q0, a.s0, nt * (a.N >> 1), a.N >> 1};
+    sg[1] = {a.q1, a.s1, nt * (a.N >> 1), a.N >> 1};
     return 2;
   }
   if (epi == TEPI_QKV) {
@@ -580,21 +580,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
           img_store8(a.out_img, mr, cb, 128, u8);
         }
       }
-    } else if (EPI == TEPI_GLU) {  // N == 256: columns j (W1) and 128 + j (W3); this thread: j in 64*half..
+    } else if (EPI == TEPI_GLU) {  // columns j (W1) and H + j (W3), H = N/2; this thread: j in (H/2)*half..
+      const int H = a.N >> 1, hq = H >> 1;
 #pragma unroll 1
-      for (int cc = 0; cc < 64; cc += 32) {
-        const int c0 = half * 64 + cc;
+      for (int cc = 0; cc < hq; cc += 32) {
+        const int c0 = half * hq + cc;
         float va[32], vb[32];
         tmem_ld32(lane_addr + c0, va);
-        tmem_ld32(lane_addr + 128 + c0, vb);
+        tmem_ld32(lane_addr + H + c0, vb);
         if (!live) continue;
 #pragma unroll
         for (int k0 = 0; k0 < 32; k0 += 8) {
           float h8[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            h8[i] = swiglu(__fmul_rn(va[k0 + i], sscale[c0 + k0 + i]), __fmul_rn(vb[k0 + i], sscale[128 + c0 + k0 + i]));
-          img_store8(a.out_img, m, nt * 128 + c0 + k0, a.out_K, h8);
+            h8[i] = swiglu(__fmul_rn(va[k0 + i], sscale[c0 + k0 + i]), __fmul_rn(vb[k0 + i], sscale[H + c0 + k0 + i]));
+          img_store8(a.out_img, m, nt * H + c0 + k0, a.out_K, h8);
         }
       }
     }
