@@ -964,6 +964,24 @@ static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st)
   const int items = ((a.n + tc::kM - 1) / tc::kM) * a.n_tiles;
   const int grid = items < sms ? items : sms;
   const size_t smem = tc::smem_bytes();
+  if (epi == tc::TEPI_RESNORM && a.pair) {
+    // one item per CTA, the two column halves of an M tile in one 2-CTA cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)items);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_RESNORM>, a);
+    if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tc_gemm_kernel launch: %s", cudaGetErrorString(e));
+    return Q6W_OK;
+  }
   switch (epi) {
     case tc::TEPI_QKV: tc::tc_gemm_kernel<tc::TEPI_QKV><<<grid, tc::kThreads, smem, st>>>(a); break;
     case tc::TEPI_RESNORM: tc::tc_gemm_kernel<tc::TEPI_RESNORM><<<grid, tc::kThreads, smem, st>>>(a); break;
@@ -972,6 +990,17 @@ static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st)
   }
   Q6W_LAUNCH_CHECK("tc_gemm_kernel");
   return Q6W_OK;
+}
+
+// RESNORM tiles (dim 128): when every M tile can have two CTAs at once, its
+// two 64-column halves run as a 2-CTA cluster (twice the CTAs, half the
+// epilogue each); otherwise one CTA takes all 128 columns.
+static void tc_resnorm_tiles(tc::TcArgs& a, int n, int sms) {
+  const int m_tiles = (n + tc::kM - 1) / tc::kM;
+  const bool pair = 2 * m_tiles <= sms;
+  a.N = pair ? 64 : 128;
+  a.n_tiles = pair ? 2 : 1;
+  a.pair = pair ? 1 : 0;
 }
 
 static int32_t tc_set_attrs() {
@@ -1034,8 +1063,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.K = dim;
       a.q0 = L.wo.packed; a.s0 = L.wo.scales;
       a.end0 = a.end1 = dim;
-      a.N = dim;
-      a.n_tiles = 1;
+      tc_resnorm_tiles(a, n, M->sm_count);
       a.x = w.x; a.gnorm = L.ffn_norm; a.out_img = w.xs_img; a.out_K = dim;
       if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st))) return rc;
     }
@@ -1057,8 +1085,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.K = hid;
       a.q0 = L.w2.packed; a.s0 = L.w2.scales;
       a.end0 = a.end1 = dim;
-      a.N = dim;
-      a.n_tiles = 1;
+      tc_resnorm_tiles(a, n, M->sm_count);
       a.x = w.x;
       a.gnorm = l + 1 < d.n_layers ? M->layers[l + 1].attention_norm : d.norm;
       a.out_img = w.xs_img; a.out_K = dim;

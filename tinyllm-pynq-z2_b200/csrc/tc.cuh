@@ -23,6 +23,7 @@
 // shared memory by the CTA itself (three 32-bit loads -> 16 bf16 codes).
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 #include "async.cuh"
@@ -191,8 +192,9 @@ struct TcArgs {
   const float* s1;
   const float* s2;
   int32_t end0, end1;  // QKV: virtual-row ends of wq and wk
-  int32_t N;           // rows per N tile (128 or 256)
+  int32_t N;           // rows per N tile (64, 128 or 256)
   int32_t n_tiles;     // N tiles per M tile
+  int32_t pair;        // RESNORM: the two 64-column tiles of an M tile run as a 2-CTA cluster
   // epilogue
   float* x;            // RESNORM: residual stream [n, 128] (read + written)
   const float* gnorm;  // RESNORM: norm weight applied to the new x for the next image
@@ -275,6 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   __shared__ int timed_out;
   __shared__ int s_ok[kM], s_pos[kM];  // QKV epilogue: per row
   __shared__ int64_t s_crow[kM];
+  __shared__ float s_ssp[kM];          // RESNORM pair: this CTA's half of each row's sum of squares
+  namespace cg = cooperative_groups;
+  int pair_synced = 0;                 // RESNORM pair: cluster barriers taken (two per item)
   const int tid = threadIdx.x, warp = tid >> 5;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;                       // [3][2][128][128 B] = 96 KB (one K stage)
@@ -513,15 +518,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
         }
         __syncthreads();  // the next block reuses sB
       }
-    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim
+    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim, or N == 64 per CTA of a pair (a.pair)
       // Two passes through shared memory (sB: the weights are consumed once the
       // MMAs are done), so every global access is row-contiguous.
-      // E1: this thread's row (TMEM lane) and columns 64*half..+63, scaled,
+      // E1: this thread's row (TMEM lane) and columns (N/2)*half.., scaled,
       // into sB as float4 unit c4 of row r at r*32 + (c4 ^ (r & 7)).
       float4* st4 = reinterpret_cast<float4*>(sB);
-#pragma unroll
-      for (int cc = 0; cc < 64; cc += 32) {
-        const int c0 = half * 64 + cc;
+      const int hn = a.N >> 1;
+      for (int cc = 0; cc < hn; cc += 32) {
+        const int c0 = half * hn + cc;
         float v[32];
         tmem_ld32(lane_addr + c0, v);
         const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
@@ -534,50 +539,85 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
         }
       }
       __syncthreads();
-      // E2: half-warps take rows (16 lanes x 8 columns = one row): residual add,
-      // x written back, the row's sum of squares over the 16 lanes, RMSNorm with
-      // the next norm weight, and the row's image units.
-      const int lane = tid & 31, sub = lane >> 4, cb = 8 * (lane & 15);
+      // E2: lane groups of N/8 lanes take rows (8 columns a lane): residual add,
+      // x written back, the row's sum of squares over the group (plus the
+      // peer's half of the row in pair mode, added in rank order), RMSNorm
+      // with the next norm weight, and the row's image units.
+      const int lane = tid & 31;
+      const int lpr = a.N >> 3, rpi = 32 / lpr;  // lanes per row, rows per warp pass
+      const int sub = lane / lpr, cl8 = lane % lpr, cb = 8 * cl8;
+      const int col = nt * a.N + cb;  // column of x and of the image
       float gw[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) gw[i] = __ldg(a.gnorm + cb + i);
-      // the residual rows of all eight passes are loaded first, so the loads overlap
-      float4 ox[kM / 16][2];
+      for (int i = 0; i < 8; ++i) gw[i] = __ldg(a.gnorm + col + i);
+      constexpr int kPass = kM / 16;  // at most 8 passes of 2 rows per warp (4 rows in pair mode)
+      const int npass = (kM / 8) / rpi;
+      // the residual rows of all passes are loaded first, so the loads overlap
+      float4 ox[kPass][2];
 #pragma unroll
-      for (int i = 0; i < kM / 16; ++i) {
-        const int64_t mr = (int64_t)mt * kM + 2 * (warp + 8 * i) + sub;
-        const float4* xr = reinterpret_cast<const float4*>(a.x + mr * 128 + cb);
-        ox[i][0] = mr < a.n ? xr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
-        ox[i][1] = mr < a.n ? xr[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < kPass; ++i) {
+        const int64_t mr = (int64_t)mt * kM + 16 * warp + rpi * i + sub;
+        const float4* xr = reinterpret_cast<const float4*>(a.x + mr * 128 + col);
+        const bool in = i < npass && mr < a.n;
+        ox[i][0] = in ? xr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ox[i][1] = in ? xr[1] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      float xk[kPass][8];
+      float ssk[kPass];
 #pragma unroll
-      for (int i = 0; i < kM / 16; ++i) {
-        const int r = 2 * (warp + 8 * i) + sub;
+      for (int i = 0; i < kPass; ++i) {
+        ssk[i] = 0.0f;
+        const int r = 16 * warp + rpi * i + sub;
         const int64_t mr = (int64_t)mt * kM + r;
-        const bool lv = mr < a.n;  // uniform over the 16 lanes of the row
-        const float4 p0 = st4[r * 32 + ((cb >> 2) ^ (r & 7))], p1 = st4[r * 32 + (((cb >> 2) + 1) ^ (r & 7))];
-        float xn[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (lv) {
-          float4* xr = reinterpret_cast<float4*>(a.x + mr * 128 + cb);
-          const float4 o0 = ox[i][0], o1 = ox[i][1];
-          xn[0] = __fadd_rn(o0.x, p0.x); xn[1] = __fadd_rn(o0.y, p0.y);
-          xn[2] = __fadd_rn(o0.z, p0.z); xn[3] = __fadd_rn(o0.w, p0.w);
-          xn[4] = __fadd_rn(o1.x, p1.x); xn[5] = __fadd_rn(o1.y, p1.y);
-          xn[6] = __fadd_rn(o1.z, p1.z); xn[7] = __fadd_rn(o1.w, p1.w);
-          xr[0] = make_float4(xn[0], xn[1], xn[2], xn[3]);
-          xr[1] = make_float4(xn[4], xn[5], xn[6], xn[7]);
+        const bool lv = i < npass && mr < a.n;  // uniform over the lanes of the row
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xk[i][e] = 0.0f;
+        if (i < npass) {
+          const float4 p0 = st4[r * 32 + ((cb >> 2) ^ (r & 7))], p1 = st4[r * 32 + (((cb >> 2) + 1) ^ (r & 7))];
+          if (lv) {
+            float4* xr = reinterpret_cast<float4*>(a.x + mr * 128 + col);
+            const float4 o0 = ox[i][0], o1 = ox[i][1];
+            xk[i][0] = __fadd_rn(o0.x, p0.x); xk[i][1] = __fadd_rn(o0.y, p0.y);
+            xk[i][2] = __fadd_rn(o0.z, p0.z); xk[i][3] = __fadd_rn(o0.w, p0.w);
+            xk[i][4] = __fadd_rn(o1.x, p1.x); xk[i][5] = __fadd_rn(o1.y, p1.y);
+            xk[i][6] = __fadd_rn(o1.z, p1.z); xk[i][7] = __fadd_rn(o1.w, p1.w);
+            xr[0] = make_float4(xk[i][0], xk[i][1], xk[i][2], xk[i][3]);
+            xr[1] = make_float4(xk[i][4], xk[i][5], xk[i][6], xk[i][7]);
+          }
         }
         float ss = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(xn[e], xn[e]));
+        for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(xk[i][e], xk[i][e]));
+        for (int o = lpr >> 1; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        ssk[i] = ss;
+        if (a.pair && i < npass && cl8 == 0) s_ssp[r] = ss;
+      }
+      if (a.pair) {
+        // both halves of every row: the partial sums meet through distributed
+        // shared memory; the second barrier keeps this CTA's array alive
+        // until the peer has read it
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        const float* peer = cl.map_shared_rank(s_ssp, nt ^ 1);
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        if (lv) {
-          const float rstd = rms_scale(ss, 128, a.eps);
+        for (int i = 0; i < kPass; ++i) {
+          if (i < npass) {
+            const int r = 16 * warp + rpi * i + sub;
+            ssk[i] = nt == 0 ? __fadd_rn(ssk[i], peer[r]) : __fadd_rn(peer[r], ssk[i]);
+          }
+        }
+        cl.sync();
+        pair_synced = 2;
+      }
+#pragma unroll
+      for (int i = 0; i < kPass; ++i) {
+        const int64_t mr = (int64_t)mt * kM + 16 * warp + rpi * i + sub;
+        if (i < npass && mr < a.n) {
+          const float rstd = rms_scale(ssk[i], 128, a.eps);
           float u8[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) u8[e] = __fmul_rn(__fmul_rn(xn[e], rstd), gw[e]);
-          img_store8(a.out_img, mr, cb, 128, u8);
+          for (int e = 0; e < 8; ++e) u8[e] = __fmul_rn(__fmul_rn(xk[i][e], rstd), gw[e]);
+          img_store8(a.out_img, mr, col, 128, u8);
         }
       }
     } else if (EPI == TEPI_GLU) {  // columns j (W1) and H + j (W3), H = N/2; this thread: j in (H/2)*half..
@@ -602,6 +642,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
     tc_fence_before();
     __syncthreads();
   }
+  // a pair CTA that stopped early still takes its two cluster barriers, so
+  // the peer's waits end
+  if (EPI == TEPI_RESNORM && a.pair)
+    for (; pair_synced < 2; ++pair_synced) cg::this_cluster().sync();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
