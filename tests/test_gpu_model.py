@@ -265,10 +265,13 @@ def test_gqa_group_kernel_matches_per_head(tiny, n, L, KV, rep, hd):
         assert (out[i] - (w @ vs).squeeze(1)).abs().max() <= 1e-5
 
 
-@pytest.mark.parametrize("n", [64, 130, 513])
+@pytest.mark.parametrize("n", [64, 130, 513, 9600])
 def test_tensor_core_step_matches_simt_step(tiny_files, monkeypatch, n):
     """The tcgen05 batched step (n >= 64) against the FP32 SIMT step on the
-    same inputs, and both against the oracle on a sample of sequences."""
+    same inputs, and both against the oracle on a sample of sequences.  Up to
+    74 tiles of 128 sequences the residual + RMSNorm GEMM runs as 2-CTA
+    clusters of column halves; 9600 sequences (75 tiles) take the one-CTA
+    form on a 148-SM B200."""
     tc_model = Q6WCudaTransformer.from_q6w(*tiny_files)
     monkeypatch.setenv("Q6W_DISABLE_TC", "1")
     simt_model = Q6WCudaTransformer.from_q6w(*tiny_files)
