@@ -21,6 +21,13 @@
 //
 // Weights are expanded from the packed int6 rows into the same layout in
 // shared memory by the CTA itself (three 32-bit loads -> 16 bf16 codes).
+//
+// Tiles.  An item is (128-sequence M tile, N-row weight tile).  QKV uses two
+// 128-row tiles (q | k v) when the rows divide, GLU tiles of 64 W1 + 64 W3
+// rows, VOCAB 256 rows; RESNORM needs whole rows for its RMSNorm and runs
+// each M tile either in one CTA (N = 128) or, when every M tile can have two
+// CTAs at once, as a 2-CTA cluster of 64-column halves that add their
+// per-row sums of squares through distributed shared memory.
 #pragma once
 
 #include <cooperative_groups.h>
