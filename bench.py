@@ -47,6 +47,10 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=128)
     ap.add_argument("--cpu-sample-requests", type=int, default=2, help="requests per CPU worker per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--verify-sample", type=int, default=512,
+                    help="sequences of the timed output teacher-forced against the oracle (all ranks together)")
+    ap.add_argument("--verify-all", action="store_true",
+                    help="teacher-force every sequence of the timed output against the oracle")
     ap.add_argument("--only-main", action="store_true", help="skip the B=1, GEMV and CPU side measurements")
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
@@ -123,6 +127,39 @@ def cpu_cores():
         return len(os.sched_getaffinity(0))
     except Exception:
         return os.cpu_count() or 1
+
+
+def _verify_chunk(job):
+    """One process: teacher-forced oracle check of a chunk of device greedy streams."""
+    bin_path, man_path, prompts, sampled, new_tokens, threads = job
+    import torch
+
+    torch.set_num_threads(threads)
+    from oracle.model import BatchScorer, OracleModel
+
+    m = OracleModel.from_q6w(bin_path, man_path)
+    return BatchScorer(m).verify_greedy(prompts, sampled, new_tokens, chunk=len(prompts))
+
+
+def verify_streams(bin_path, man_path, prompts, sampled, new_tokens, workers):
+    """Teacher-force device greedy streams through the oracle (BatchScorer) in
+    `workers` spawned processes; every pick must be the oracle's argmax or an
+    FP32 near-tie within 1e-4 of its maximum, and every stream full length."""
+    import multiprocessing as mp
+
+    n = len(prompts)
+    workers = max(1, min(workers, n))
+    per = (n + workers - 1) // workers
+    jobs = [(str(bin_path), str(man_path), prompts[i: i + per], sampled[i: i + per], new_tokens, 1)
+            for i in range(0, n, per)]
+    with mp.get_context("spawn").Pool(len(jobs)) as pool:
+        res = pool.map(_verify_chunk, jobs)
+    # failures carry chunk-local sequence indexes: make them indexes into `prompts`
+    fails = [(f[0] + c * per,) + tuple(f[1:]) for c, r in enumerate(res) for f in r["failures"]]
+    return {"checked": n, "picks": sum(r["picks"] for r in res), "exact": sum(r["exact"] for r in res),
+            "near_ties": sum(r["near_ties"] for r in res), "failures": len(fails),
+            "first_failures": [list(map(str, f)) for f in fails[:5]],
+            "min_margin": min(r["min_margin"] for r in res)}
 
 
 def run_reference(a):
@@ -294,8 +331,19 @@ def run_b200(a):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    # ---- correctness of the timed output: full length and a teacher-forced oracle check on a sample
+    # ---- correctness of the timed output (the last end-to-end step's ids, now in out_host): a seeded
+    # sample of the sequences (every sequence with --verify-all) teacher-forced through the oracle
     ok_len = bool((n_sampled == T).all().item())
+    import random
+
+    share = n if a.verify_all else min(n, max(1, a.verify_sample // world))
+    pick = sorted(random.Random(4242 + rank).sample(range(n), share))
+    hp = host_prompts.tolist()
+    hs = out_host.tolist()
+    t_v = time.perf_counter()
+    par = verify_streams(b, m, [hp[i] for i in pick], [hs[i] for i in pick], T,
+                         max(1, cpu_cores() // world))
+    par["seconds"] = round(time.perf_counter() - t_v, 1)
 
     # ---- dominant kernel alone: decode attention over this run's caches
     roof = attention_roofline(model, caches, n, P + T - 1, stream)
@@ -308,9 +356,20 @@ def run_b200(a):
     pf = prefill_c3(model, rank, world, stream) if side else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    cnt = torch.tensor([par["checked"], par["picks"], par["exact"], par["near_ties"], par["failures"]],
+                       dtype=torch.float64, device=dev)
+    mm = torch.tensor([par["min_margin"]], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(cnt, op=dist.ReduceOp.SUM)
+        dist.all_reduce(mm, op=dist.ReduceOp.MIN)
     ms, e2e_ms = float(t[0]), float(t[1])
+    parity = {"checked_sequences": int(cnt[0]), "of_sequences": n * world, "picks": int(cnt[1]),
+              "exact": int(cnt[2]), "near_ties": int(cnt[3]), "failures": int(cnt[4]),
+              "min_top1_top2_margin": round(float(mm[0]), 6),
+              "method": "teacher-forced oracle (BatchScorer) over prompt + all generated tokens; a pick passes "
+                        "if it is the oracle argmax or within 1e-4 of the oracle maximum",
+              "rank0_first_failures": par["first_failures"], "rank0_seconds": par["seconds"]}
     total_tokens = n * T * a.steps * world
     value = total_tokens / (ms / 1e3)
     e2e_value = total_tokens / (e2e_ms / 1e3)
@@ -324,7 +383,7 @@ def run_b200(a):
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(n * P * 4),
                     "d2h_bytes_per_step": int(n * T * 4)},
             "gpu_launches": launches_per_gen * a.steps,
-            "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len,
+            "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len, "parity": parity,
             "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1, "prefill": pf,
         }
         if not a.no_cpu_baseline and not a.only_main and world == 1:
@@ -568,8 +627,8 @@ def profile_scaled_step(n=1):
 
 
 def profile_gemv(shape):
-    """One B=1 GEMV shape, 4 launches on random data: the small case the
-    ncu summaries under profiles/ are taken on."""
+    """One B=1 GEMV shape, 4 launches on random data: a small case for an
+    ncu capture of the streaming GEMV."""
     import torch
 
     from q6w_b200 import _lib
@@ -620,13 +679,16 @@ def attention_roofline(model, caches, n, length, stream):
     nbytes = 2 * n * length * KV * hd * 4 + 2 * n * H * hd * 4
     peak, kind = measured_peaks()
     ach = nbytes / sec / 1e9
-    # DRAM bytes of one launch from ncu (profiles/attn_warp_tiny_2048seq_len147.md: 159.89 MB read +
-    # written at 2048 sequences, length 147), scaled by the sequence count
-    traffic = int(159.89e6 * n / 2048) if length == 147 else None
+    # DRAM bytes (read + written) of one launch as ncu measured them on a smaller capture of the same
+    # kernel: 2048 sequences at length 147 moved 159.89 MB; traffic grows with the sequence count
+    ncu_bytes, ncu_seqs, ncu_len = 159.89e6, 2048, 147
+    traffic = int(ncu_bytes * n / ncu_seqs) if length == ncu_len else None
     return {"kernel": "attn_warp_kernel (decode GQA attention, timed alone)", "bound": "hbm",
             "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-            "peak_kind": f"{kind} hbm_gbs (copy, burst)", "traffic": traffic, "bytes_per_launch": nbytes,
-            "us_per_launch": round(sec * 1e6, 2)}
+            "peak_kind": f"{kind} hbm_gbs (copy, burst)", "traffic": traffic,
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at {ncu_seqs} "
+                               f"sequences, length {ncu_len}, scaled by sequences ({n})") if traffic else None,
+            "bytes_per_launch": nbytes, "us_per_launch": round(sec * 1e6, 2)}
 
 
 def main():

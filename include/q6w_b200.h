@@ -64,6 +64,19 @@ Q6W_API int32_t q6w_unpack(const uint8_t* packed, int8_t* out, int64_t rows, int
 Q6W_API int32_t q6w_dequant(const uint8_t* packed, const float* scales, float* out, int64_t rows,
                     int64_t cols, q6w_stream_t stream);
 
+/* The Q6W writer's row-wise quantization on the GPU: quantize_rows +
+ * pack_signed_int6 (quantization/q6w_format.py:84-98, 52-64) with the same
+ * FP32 operations, so codes and scales are bit-identical to the reference:
+ * scales[r] = max|w[r,:]| / 31 (1.0 for an all-zero row), codes =
+ * clamp(round-half-even(w / scale), -31, 31), packed into rows*cols*3/4
+ * bytes.  weights [rows, cols] FP32 (finite; the caller checks), cols % 4 == 0.
+ * row_err ([rows][3] FP64 scratch) and stats (3 FP64: max_abs_error,
+ * mean_abs_error, rmse of q*scale - w) are optional (NULL); stats needs
+ * row_err.  The statistics sum in FP64 in a fixed order, so they agree with
+ * the reference's FP32 torch reductions to within their rounding. */
+Q6W_API int32_t q6w_quantize_rows(const float* weights, int64_t rows, int64_t cols, uint8_t* packed,
+                                  float* scales, double* row_err, double* stats, q6w_stream_t stream);
+
 /* ---- linear ------------------------------------------------------------ */
 
 /* y[n, rows] = x[n, cols] @ W^T with W = dequant(packed, scales): the
@@ -92,9 +105,12 @@ Q6W_API int32_t q6w_linear_argmax(const uint8_t* packed, const float* scales, co
  * cudaMalloc can fail and cudaFree synchronises the device.  The argmax keys
  * live in a library-owned device array of 32768 entries (256 KiB, held by
  * every GPU that loads the library until exit), so n <= 32768; larger n is
- * rejected with Q6W_ERR_ARG.  Allocates nothing.  The first call on each
- * device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture.  All calls share the one array
+ * rejected with Q6W_ERR_ARG.  Allocates nothing.  The first call in each
+ * CUDA context (each device's primary context, and again after a
+ * cudaDeviceReset or when the caller makes another context current) looks
+ * up the array's device address in that context (cudaGetSymbolAddress) and
+ * caches it under the context's id; make that first call before any stream
+ * capture.  All calls share the one array
  * (cleared at the start of each call): calls that overlap on the GPU, on
  * any streams, race and must be serialised by the caller. */
 Q6W_API int32_t q6w_linear_argmax_noalloc(const uint8_t* packed, const float* scales,

@@ -65,31 +65,35 @@ def tiny_files(tmp_path_factory, golden_tiny):
     return b, m
 
 
-@pytest.fixture(scope="session")
-def shipped_files(golden_shipped):
-    """The shipped QAT artifact, when available: $Q6W_SHIPPED_DIR or the
-    reference checkout in $Q6W_REFERENCE.  Skips otherwise."""
-    name = golden_shipped["binary_file"]
+def _shipped_candidates():
+    """Directories that may hold the shipped QAT artifact: $Q6W_SHIPPED_DIR,
+    the artifacts folder of a reference checkout named by $Q6W_REFERENCE, and
+    tests/golden/shipped/ (an uncommitted local copy made by
+    ``tests/golden/make_golden.py --copy-shipped``)."""
     cands = []
     if os.environ.get("Q6W_SHIPPED_DIR"):
         cands.append(Path(os.environ["Q6W_SHIPPED_DIR"]))
-    # the reference checkout, when this machine has one (read-only)
-    cands.append(Path(os.environ.get("Q6W_REFERENCE", "/root/reference")) / "quantization" / "artifacts")
-    for c in cands:
-        b, m = c / name, c / name.replace(".bin", ".json")
-        if b.exists() and m.exists():
-            return b, m
-    pytest.skip("shipped Q6W artifact not available (set Q6W_SHIPPED_DIR)")
+    if os.environ.get("Q6W_REFERENCE"):
+        cands.append(Path(os.environ["Q6W_REFERENCE"]) / "quantization" / "artifacts")
+    cands.append(GOLDEN / "shipped")
+    return cands
 
 
 @pytest.fixture(scope="session")
-def shipped_files_env(golden_shipped):
-    """The shipped QAT artifact from $Q6W_SHIPPED_DIR only (GPU tests); skips otherwise."""
+def shipped_files(golden_shipped):
+    """The shipped QAT artifact (binary + manifest); skips when no copy is found."""
     name = golden_shipped["binary_file"]
-    d = os.environ.get("Q6W_SHIPPED_DIR")
-    if d and (Path(d) / name).exists():
-        return Path(d) / name, Path(d) / name.replace(".bin", ".json")
-    pytest.skip("shipped Q6W artifact not available (set Q6W_SHIPPED_DIR)")
+    for c in _shipped_candidates():
+        b, m = c / name, c / name.replace(".bin", ".json")
+        if b.exists() and m.exists():
+            return b, m
+    pytest.skip("shipped Q6W artifact not available (set Q6W_SHIPPED_DIR or run make_golden.py --copy-shipped)")
+
+
+@pytest.fixture(scope="session")
+def shipped_files_env(shipped_files):
+    """The shipped QAT artifact for the GPU tests (same lookup)."""
+    return shipped_files
 
 
 def small_model_files(tmp_path_factory, args, seed, tag):

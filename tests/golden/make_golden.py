@@ -1,9 +1,15 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-``$Q6W_REFERENCE`` (default /root/reference):
+Run in a container that has the reference checkout (read-only); its path
+is required in ``$Q6W_REFERENCE``:
 
-    python tests/golden/make_golden.py
+    Q6W_REFERENCE=<checkout> python tests/golden/make_golden.py
+    Q6W_REFERENCE=<checkout> python tests/golden/make_golden.py --copy-shipped
+
+``--copy-shipped`` only copies the shipped QAT artifact (binary + manifest,
+1.1 MB, public) into ``tests/golden/shipped/``, which git ignores: the GPU
+test of the shipped request finds it there on a machine without the
+checkout, and it is never committed.
 
 It imports the reference's own ``quantization/q6w_format.py`` and
 ``benchmarks/torch_benchmark.py`` and records what they produce:
@@ -41,7 +47,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("Q6W_REFERENCE", "/root/reference"))
+if not os.environ.get("Q6W_REFERENCE"):
+    sys.exit("set Q6W_REFERENCE to the reference checkout")
+REF = Path(os.environ["Q6W_REFERENCE"])
 sys.path.insert(0, str(REPO / "tinyllm-pynq-z2_b200"))
 sys.path.insert(0, str(REF / "quantization"))
 sys.path.insert(0, str(REF / "benchmarks"))
@@ -173,7 +181,23 @@ def shipped_request():
             "margins": run["margins"], "torch": torch.__version__}
 
 
+SHIPPED = "tinyllamas_zh_story_q6w_qat_lr1e6"
+
+
+def copy_shipped():
+    import shutil
+
+    dst = HERE / "shipped"
+    dst.mkdir(exist_ok=True)
+    for ext in (".bin", ".json"):
+        shutil.copyfile(REF / "quantization" / "artifacts" / (SHIPPED + ext), dst / (SHIPPED + ext))
+    print("shipped artifact copied to", dst)
+
+
 def main():
+    if "--copy-shipped" in sys.argv:
+        copy_shipped()
+        return
     torch.set_num_threads(1)
     (HERE / "codec.json").write_text(json.dumps(codec_vectors(), indent=1) + "\n")
     with tempfile.TemporaryDirectory() as d:

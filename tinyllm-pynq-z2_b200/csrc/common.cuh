@@ -30,6 +30,11 @@ void clear_error();
   } while (0)
 
 int sm_count();
+// Id of the CUDA context current on this host thread (0 if none / unknown).
+unsigned long long context_id();
+// Device address of a __device__ symbol in the current context, looked up
+// once per (context, symbol) and cached.
+cudaError_t symbol_address(const void* symbol, void** out);
 namespace stream {
 int32_t* error_word();
 }
@@ -85,8 +90,12 @@ __device__ __forceinline__ uint32_t load_group(const uint8_t* p) {
 }
 
 // Order-preserving 32-bit image of a float (larger float -> larger key).
+// Every NaN maps to the canonical +NaN first, so it ranks above +inf as
+// torch.argmax ranks NaN (a NaN with the sign bit set would otherwise sort
+// below -inf).  Every float then has a key > 0: a key of 0 means "no value
+// seen", which argmax_index turns into -1.
 __device__ __forceinline__ uint32_t float_key(float v) {
-  uint32_t u = __float_as_uint(v);
+  uint32_t u = v != v ? 0x7FC00000u : __float_as_uint(v);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 

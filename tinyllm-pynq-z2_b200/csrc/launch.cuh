@@ -70,7 +70,9 @@ struct LinearLauncher {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, x, g, eps, ms, ep, geo, stream::error_word());
+    int32_t* err = stream::error_word();
+    if (!err) return cudaErrorInvalidSymbol;  // the kernel's timeout diagnostic needs its device address
+    return cudaLaunchKernelEx(&cfg, kern, x, g, eps, ms, ep, geo, err);
   }
 
   static cudaError_t stream_launch(const float* x, const float* g, float eps, const MatSet& ms, const EpiArgs& ep,

@@ -154,30 +154,43 @@ namespace q6w {
 constexpr int64_t kNoAllocMaxRows = 32768;  // activation rows per call
 static __device__ __align__(256) unsigned long long g_noalloc_keys[kNoAllocMaxRows];
 
-// Device address of g_noalloc_keys, looked up once per device (the host-side
-// name is only a stand-in for the symbol, not a device pointer).
+// Device address of g_noalloc_keys (the host-side name is only a stand-in
+// for the symbol, not a device pointer).  The address belongs to the CUDA
+// context that loaded this module, so it is looked up with cudaGetSymbolAddress
+// once per context -- the first call on each device, and again after the
+// context changes (a cudaDeviceReset, or a driver-API context the caller made
+// current) -- and cached under the context's unique id.
 static unsigned long long* noalloc_keys_ptr(int32_t* status) {
+  struct Entry {
+    unsigned long long ctx;
+    unsigned long long* ptr;
+  };
   static std::mutex mu;
-  static unsigned long long* ptrs[64] = {nullptr};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    *status = fail(Q6W_ERR_CUDA, "q6w_linear_argmax_noalloc: cannot query the current device");
+  static Entry cache[64];
+  static int used = 0;
+  unsigned long long ctx = context_id();
+  if (ctx) {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].ctx == ctx) {
+        *status = Q6W_OK;
+        return cache[i].ptr;
+      }
+  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_keys);
+  if (e != cudaSuccess || !p) {
+    *status = fail(Q6W_ERR_CUDA, "q6w_linear_argmax_noalloc: cudaGetSymbolAddress failed: %s",
+                   cudaGetErrorString(e));
     return nullptr;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_keys);
-    if (e != cudaSuccess || !p) {
-      *status = fail(Q6W_ERR_CUDA, "q6w_linear_argmax_noalloc: cudaGetSymbolAddress failed: %s",
-                     cudaGetErrorString(e));
-      return nullptr;
-    }
-    ptrs[dev] = (unsigned long long*)p;
+  if (!ctx) ctx = context_id();  // the lookup made the primary context current
+  if (ctx) {
+    std::lock_guard<std::mutex> lock(mu);
+    cache[used < 64 ? used++ : (int)(ctx % 64)] = {ctx, (unsigned long long*)p};
   }
   *status = Q6W_OK;
-  return ptrs[dev];
+  return (unsigned long long*)p;
 }
 
 }  // namespace q6w

@@ -143,12 +143,32 @@ def ffn_dim(args):
     return multiple * ((h + multiple - 1) // multiple)
 
 
-def write_q6w(state, model_args, output_path, manifest_path, provenance=None, overwrite=False):
+def _quantize_on_device(t, device):
+    """GPU quantize + pack of one matrix, with the writer's self-check done on
+    the device: every code dequantizes to within half a scale step of its
+    weight (the round-trip check of the host path, without a host unpack).
+    The bound allows the FP32 roundings of w / scale (ratios up to 31, so up
+    to 31 * 2^-24 of a step) and of q * scale."""
+    from . import ops
+
+    w = t.detach().to(device=device, dtype=torch.float32).contiguous()
+    packed, scales, stats = ops.quantize_rows(w, device)
+    rows, cols = w.shape
+    deq = ops.dequantize_rows(packed, scales, rows, cols)
+    if not bool(((deq - w).abs() <= scales[:, None] * (0.5 + 1e-5)).all()):
+        raise AssertionError("Q6 device quantization self-check failed")
+    return packed.cpu().numpy().tobytes(), scales.cpu().numpy().astype("<f4", copy=False), stats
+
+
+def write_q6w(state, model_args, output_path, manifest_path, provenance=None, overwrite=False, device=None):
     """Write ``state`` (FP32 tensors by name) as a Q6W binary + manifest.
 
     Section order, alignment, header and manifest schema follow
     ``export_q6w`` (q6w_format.py:134-227).  Every quantized tensor is
-    round-trip checked after packing.  Returns the manifest dict.
+    round-trip checked after packing.  With ``device`` a CUDA device, the
+    quantization and packing run on that GPU (``ops.quantize_rows``: same
+    codes, scales and bytes; error statistics summed in FP64).  Returns the
+    manifest dict.
     """
     output_path, manifest_path = Path(output_path), Path(manifest_path)
     if not overwrite and (output_path.exists() or manifest_path.exists()):
@@ -176,10 +196,13 @@ def write_q6w(state, model_args, output_path, manifest_path, provenance=None, ov
                 raise ValueError(f"Unsupported quantized tensor shape for {key}: {tuple(t.shape)}")
             if not torch.isfinite(t).all():
                 raise ValueError(f"Non-finite values found in {key}")
-            q, scales, stats = quantize_rows(t)
-            packed = pack_signed_int6(q)
-            if not np.array_equal(_unpack_host(packed, *t.shape), q):
-                raise AssertionError(f"Q6 pack/unpack self-check failed for {key}")
+            if device is not None and torch.device(device).type == "cuda":
+                packed, scales, stats = _quantize_on_device(t, device)
+            else:
+                q, scales, stats = quantize_rows(t)
+                packed = pack_signed_int6(q)
+                if not np.array_equal(_unpack_host(packed, *t.shape), q):
+                    raise AssertionError(f"Q6 pack/unpack self-check failed for {key}")
             sb = scales.tobytes()
             s_off = put(sb)
             d_off = put(packed)
@@ -342,12 +365,16 @@ def synthetic_state(model_args, seed, std=0.02):
     return state
 
 
-def write_synthetic(model_args, seed, output_path, manifest_path, std=0.02, overwrite=False):
-    """Generate a seeded synthetic model and write it as Q6W; returns the manifest."""
+def write_synthetic(model_args, seed, output_path, manifest_path, std=0.02, overwrite=False, device=None):
+    """Generate a seeded synthetic model and write it as Q6W; returns the manifest.
+
+    The weights are always drawn on the host generator (the seed fixes the
+    model); ``device`` moves the quantization and packing to that GPU.
+    """
     state = synthetic_state(model_args, seed, std)
     prov = {"synthetic": {"seed": int(seed), "init": f"normal(0, {std}) per quantized tensor, "
                           "torch.Generator(cpu).manual_seed(seed), drawn in file order; norms = 1.0"}}
-    return write_q6w(state, model_args, output_path, manifest_path, prov, overwrite=overwrite)
+    return write_q6w(state, model_args, output_path, manifest_path, prov, overwrite=overwrite, device=device)
 
 
 class RandomImage:

@@ -60,6 +60,36 @@ def dequantize_rows(packed, scales, rows, columns):
     return out
 
 
+def quantize_rows(tensor, device="cuda"):
+    """Row-wise int6 quantization + packing on the GPU: the device half of the
+    Q6W writer (quantization/q6w_format.py:84-98 and 52-64).
+
+    Codes and scales are bit-identical to the reference's ``quantize_rows``
+    (same FP32 division and round-half-even); the codes come back already
+    packed.  Returns (packed uint8 [rows*cols*3/4], scales float32 [rows],
+    stats dict) with packed/scales on ``device``; the stats are summed in
+    FP64 and agree with the reference's FP32 reductions to their rounding.
+    """
+    device = _dev(device)
+    w = tensor.detach().to(device=device, dtype=torch.float32).contiguous()
+    if w.ndim != 2:
+        raise ValueError("Per-output-row quantization requires a matrix")
+    rows, cols = w.shape
+    if cols % 4:
+        raise ValueError("Q6 rows must be 2D and have a width divisible by four")
+    packed = torch.empty(rows * cols * 3 // 4, dtype=torch.uint8, device=device)
+    scales = torch.empty(rows, dtype=torch.float32, device=device)
+    row_err = torch.empty((max(rows, 1), 3), dtype=torch.float64, device=device)
+    stats = torch.zeros(3, dtype=torch.float64, device=device)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        _lib.check(lib.q6w_quantize_rows(w.data_ptr(), rows, cols, packed.data_ptr(), scales.data_ptr(),
+                                         row_err.data_ptr(), stats.data_ptr(), _lib.stream_handle()),
+                   "q6w_quantize_rows")
+    st = stats.tolist()
+    return packed, scales, {"max_abs_error": st[0], "mean_abs_error": st[1], "rmse": st[2]}
+
+
 def q6w_linear(x, packed, scales, rows, columns):
     """``x @ dequant(W).T`` for x [..., columns] FP32 on the GPU -> [..., rows]."""
     if x.dtype != torch.float32 or x.shape[-1] != columns:
