@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--only-main", action="store_true", help="skip the B=1, GEMV and CPU side measurements")
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
+    ap.add_argument("--sweep-only", action="store_true", help="only run the isolated linear sweep and print it")
     ap.add_argument("--profile-scaled-step", type=int, nargs="?", const=1, default=None, metavar="N",
                     help="only run N short requests (2 + 3 tokens, default N=1) of the 1.1B-shape config and exit")
     return ap.parse_args()
@@ -354,6 +355,7 @@ def run_b200(a):
     gemv = scaled_gemv(dev, stream) if side else None
     sb1 = scaled_b1(dev, stream) if side else None
     pf = prefill_c3(model, rank, world, stream) if side else None
+    sweep = linear_sweep(dev, stream) if side else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     cnt = torch.tensor([par["checked"], par["picks"], par["exact"], par["near_ties"], par["failures"]],
@@ -384,7 +386,7 @@ def run_b200(a):
                     "d2h_bytes_per_step": int(n * T * 4)},
             "gpu_launches": launches_per_gen * a.steps,
             "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len, "parity": parity,
-            "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1, "prefill": pf,
+            "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1, "prefill": pf, "linear_sweep": sweep,
         }
         if not a.no_cpu_baseline and not a.only_main and world == 1:
             cores = cpu_cores()
@@ -508,6 +510,147 @@ def scaled_gemv(dev, stream, reps=10):
             "vocab_32000x2048": {"us_per_launch": round(vsec * 1e6, 2), "bytes": vbytes,
                                  "achieved_gbs": round(vbytes / vsec / 1e9, 1),
                                  "frac": round(vbytes / vsec / 1e9 / peak, 4)}}
+
+
+def l2_copy_gbs(dev, stream, mb=24, reps=50):
+    """L2 bandwidth microbenchmark: a copy between two `mb` MB buffers (their
+    sum well inside the 126 MB L2), repeated; (read + write bytes) / time."""
+    import torch
+
+    a = torch.randn(mb * 262144, device=dev)
+    b = torch.empty_like(a)
+    for _ in range(5):
+        b.copy_(a)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        b.copy_(a)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    del a, b
+    return 2 * mb * 2 ** 20 / sec / 1e9
+
+
+def _graph_time(call, reps, stream):
+    """Device seconds per call of `call(stream)`: `reps` calls captured in one
+    CUDA graph (no host launch cost between them), replayed after warm-up."""
+    import torch
+
+    side = torch.cuda.Stream()
+    for _ in range(3):
+        call(stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for _ in range(reps):
+            call(side)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
+SWEEP_SHAPES = [(128, 128), (64, 128), (384, 128), (128, 384), (4096, 128)]
+SWEEP_BATCHES = [1, 8, 64, 512, 4096]
+
+
+def _cpu_linear_ms(w, x, threads, budget_s=0.3):
+    """torch CPU FP32 x @ W.T (the reference's nn.Linear on dequantized
+    weights) at `threads` threads: median ms of repeated calls."""
+    import torch
+
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        x @ w.T
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+            t0 = time.perf_counter()
+            x @ w.T
+            times.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(old)
+    return statistics.median(times) * 1e3
+
+
+def linear_sweep(dev, stream):
+    """Isolated Q6W linear sweep on the tiny model's shapes: out x in of
+    128x128, 64x128, 384x128, 128x384, 4096x128, activation batch N in
+    {1, 8, 64, 512, 4096}; int6 codes U[-32, 31], row scales U(0.001, 0.05),
+    x ~ N(0, 1).  Each point times the public linear op (FP32 kernels for
+    N <= 8, tcgen05 tensor cores from N = 16) with CUDA events, repeated
+    calls on the same (L2-resident) operands.
+
+    Algorithmic work per call: bytes = rows*cols*3/4 + 4*rows + 4*N*cols +
+    4*N*rows, flops = 2*N*rows*cols (FP32-equivalent; the tensor-core path
+    issues 3x that in bf16 MMAs, one per part of x).  Roofline time =
+    max(bytes / measured L2 copy bandwidth, tensor flops / measured bf16
+    peak); `frac` = roofline time / measured time.  The CPU leg is torch
+    FP32 x @ W.T on the dequantized weights at 1 thread and all cores."""
+    import numpy as np
+    import torch
+
+    from q6w_b200 import _lib, ops
+
+    lib = _lib.load()
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    l2 = l2_copy_gbs(dev, stream)
+    cores = cpu_cores()
+    rng = np.random.default_rng(2)
+    points = []
+    for rows, cols in SWEEP_SHAPES:
+        q = rng.integers(-32, 32, size=(rows, cols))
+        sc = rng.uniform(0.001, 0.05, size=rows).astype(np.float32)
+        u = (q.astype(np.int32) & 0x3F).reshape(rows, -1, 4)
+        word = u[..., 0] | (u[..., 1] << 6) | (u[..., 2] << 12) | (u[..., 3] << 18)
+        packed = torch.from_numpy(word.astype("<u4").view(np.uint8).reshape(word.shape + (4,))[..., :3].copy()
+                                  .reshape(-1)).to(dev)
+        scales = torch.from_numpy(sc).to(dev)
+        w_cpu = torch.from_numpy(q.astype(np.float32) * sc[:, None])
+        for n in SWEEP_BATCHES:
+            x_cpu = torch.from_numpy(rng.standard_normal((n, cols)).astype(np.float32))
+            x = x_cpu.to(dev)
+            y = torch.empty((n, rows), device=dev)
+            need = ops.linear_workspace_bytes(rows, cols, n)
+            tc = need > 0
+            ws = ops._linear_workspace(dev, need) if tc else None
+            reps = 200 if n <= 512 else 50
+
+            def call(st, tensor_cores=True):
+                h = _lib.stream_handle(st)
+                if tensor_cores and tc:
+                    _lib.check(lib.q6w_linear_ex(packed.data_ptr(), scales.data_ptr(), x.data_ptr(), y.data_ptr(),
+                                                 rows, cols, n, ws.data_ptr(), ws.numel(), h))
+                else:
+                    _lib.check(lib.q6w_linear(packed.data_ptr(), scales.data_ptr(), x.data_ptr(), y.data_ptr(),
+                                              rows, cols, n, h))
+
+            sec = _graph_time(call, reps, stream)
+            nbytes = rows * cols * 3 // 4 + 4 * rows + 4 * n * cols + 4 * n * rows
+            flops = 2 * n * rows * cols
+            tflops_issued = (3 if tc else 1) * flops
+            t_roof = max(nbytes / (l2 * 1e9), (tflops_issued / (bf16 * 1e12)) if tc else 0.0)
+            pt = {"rows": rows, "cols": cols, "n": n, "kernel": "tcgen05" if tc else "fp32",
+                  "us": round(sec * 1e6, 3), "gbs": round(nbytes / sec / 1e9, 1),
+                  "tflops_fp32_equiv": round(flops / sec / 1e12, 3),
+                  "bound": "tensor" if tc and tflops_issued / (bf16 * 1e12) > nbytes / (l2 * 1e9) else "l2",
+                  "frac": round(t_roof / sec, 4)}
+            if tc:
+                pt["fp32_kernel_us"] = round(_graph_time(lambda st: call(st, False), reps, stream) * 1e6, 3)
+            pt["cpu_1t_ms"] = round(_cpu_linear_ms(w_cpu, x_cpu, 1), 4)
+            pt["cpu_all_ms"] = round(_cpu_linear_ms(w_cpu, x_cpu, cores), 4)
+            points.append(pt)
+    return {"workload": "isolated Q6W linear sweep (tiny-model shapes x N in {1, 8, 64, 512, 4096}), "
+                        "operands L2-resident across repeated calls",
+            "l2_copy_gbs": round(l2, 1), "bf16_peak_tflops": bf16, "cpu_cores": cores, "points": points}
 
 
 def prefill_c3(model, rank, world, stream, reps=3):
@@ -695,6 +838,12 @@ def main():
     a = parse()
     if a.profile_gemv:
         profile_gemv(a.profile_gemv)
+    elif a.sweep_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"linear_sweep": linear_sweep(torch.device("cuda", 0), torch.cuda.current_stream())}),
+              flush=True)
     elif a.profile_scaled_step:
         profile_scaled_step(a.profile_scaled_step)
     elif a.impl == "reference":

@@ -86,6 +86,27 @@ Q6W_API int32_t q6w_quantize_rows(const float* weights, int64_t rows, int64_t co
 Q6W_API int32_t q6w_linear(const uint8_t* packed, const float* scales, const float* x, float* y,
                    int64_t rows, int64_t cols, int64_t n, q6w_stream_t stream);
 
+/* Workspace bytes q6w_linear_ex needs to run [rows, cols] x n on the tensor
+ * cores, or 0 when that shape takes q6w_linear's FP32 kernels (n < 16, cols
+ * not a multiple of 128 or above 8192, odd rows). */
+Q6W_API size_t q6w_linear_workspace_bytes(int64_t rows, int64_t cols, int64_t n);
+
+/* q6w_linear for batches -- the same nn.Linear calls (torch_benchmark.py:105-107,
+ * 121, 123, 125) as a dense contraction on the tcgen05 tensor cores: x is
+ * written once into the workspace as three bf16 parts (hi + mid + lo hold
+ * every FP32 significand bit), the int6 codes are exact in bf16, products are
+ * exact and accumulate in FP32 in tensor memory, and the row scale multiplies
+ * each finished dot product.  The result agrees with the FP64 dequant-then-
+ * matmul to within 1e-4 * sum_k |w_k x_k| per element (tensor-core
+ * accumulation order; q6w_linear's FP32 kernels: 1e-5).  workspace: device,
+ * 256-byte aligned, q6w_linear_workspace_bytes(rows, cols, n) bytes; its
+ * first word is the error word q6w_workspace_status reads.  With a NULL
+ * workspace, or a shape / alignment the tensor-core kernel does not take
+ * (packed 16-byte aligned, x 16-byte, y 8-byte), this is q6w_linear. */
+Q6W_API int32_t q6w_linear_ex(const uint8_t* packed, const float* scales, const float* x, float* y,
+                              int64_t rows, int64_t cols, int64_t n, void* workspace,
+                              size_t workspace_bytes, q6w_stream_t stream);
+
 /* Vocab projection + greedy pick: logits = x @ W^T (optional, may be NULL)
  * and argmax[n] = first index of each row's maximum (torch.argmax), fused --
  * the tied-embedding classifier of torch_benchmark.py:125 with the greedy

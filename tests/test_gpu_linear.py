@@ -3,6 +3,11 @@ FP64 dequant-then-matmul reference and torch FP32.
 
 Tolerance (FP32 path): |y - y64| <= 1e-5 * sum_k |w_k x_k| + 1e-30 per
 element, i.e. FP32 summation error relative to the magnitude of the terms.
+Batches of 16+ rows at widths that are multiples of 128 run on the tcgen05
+tensor cores (three bf16 parts of x, exact products, FP32 accumulation in
+tensor memory in the tensor core's order): the stated, looser tolerance
+there is 1e-4 * sum_k |w_k x_k| per element, plus a relative RMS error
+below 1e-5 over the whole output.
 """
 
 import numpy as np
@@ -17,6 +22,8 @@ pytestmark = pytest.mark.gpu
 SHAPES = [(128, 128), (64, 128), (384, 128), (128, 384), (4096, 128)]
 BATCHES = [1, 8, 64, 512, 4096]
 REL = 1e-5
+REL_TC = 1e-4
+RMS_TC = 1e-5
 
 
 def make(rows, cols, n, seed):
@@ -28,24 +35,61 @@ def make(rows, cols, n, seed):
     return q, s, x, packed
 
 
-def check(y, q, s, x):
+def check(y, q, s, x, rel=REL, rms=None):
     w = codec.dequantize(q, s).astype(np.float64)
     y64 = x.astype(np.float64) @ w.T
     mag = np.abs(x.astype(np.float64)) @ np.abs(w).T
     err = np.abs(y.astype(np.float64) - y64)
-    assert (err <= REL * mag + 1e-30).all(), float((err / (mag + 1e-30)).max())
+    assert (err <= rel * mag + 1e-30).all(), float((err / (mag + 1e-30)).max())
+    if rms is not None:
+        assert np.sqrt((err ** 2).mean() / max((y64 ** 2).mean(), 1e-300)) <= rms
+    return float((err / (mag + 1e-30)).max())
+
+
+def uses_tensor_cores(rows, cols, n):
+    return ops.linear_workspace_bytes(rows, cols, n) > 0
 
 
 @pytest.mark.parametrize("rows,cols", SHAPES)
 @pytest.mark.parametrize("n", BATCHES)
 def test_linear_sweep(rows, cols, n):
+    """The public op on every sweep point: FP32 kernels for n <= 8, tensor cores for n >= 64."""
     q, s, x, packed = make(rows, cols, n, rows * 7 + cols * 3 + n)
+    tc = uses_tensor_cores(rows, cols, n)
+    assert tc == (n >= 64)
     y = ops.q6w_linear(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols)
     torch.cuda.synchronize()
     y = y.cpu().numpy()
+    check(y, q, s, x, REL_TC if tc else REL, RMS_TC if tc else None)
+    # against torch's own FP32 matmul, whose rounding is of the same order as ours:
+    # 2e-5 of sum |w x| per element (torch alone sits ~1e-6 of it from FP64)
+    w32 = torch.from_numpy(codec.dequantize(q, s))
+    ref32 = (torch.from_numpy(x) @ w32.T).numpy()
+    mag = (torch.from_numpy(np.abs(x)) @ w32.abs().T).numpy()
+    assert (np.abs(y - ref32) <= 2e-5 * mag + 1e-30).all()
+
+
+@pytest.mark.parametrize("rows,cols", SHAPES)
+@pytest.mark.parametrize("n", [64, 512])
+def test_linear_sweep_fp32_kernels(rows, cols, n):
+    """The FP32 SIMT GEMM on the batched sweep points (tensor cores off) keeps the FP32 tolerance."""
+    q, s, x, packed = make(rows, cols, n, rows * 5 + cols + n)
+    y = ops.q6w_linear(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols,
+                       tensor_cores=False).cpu().numpy()
     check(y, q, s, x)
-    ref32 = torch.from_numpy(x) @ torch.from_numpy(codec.dequantize(q, s)).T
-    assert np.abs(y - ref32.numpy()).max() <= 1e-4
+
+
+@pytest.mark.parametrize("rows,cols,n", [(64, 256, 16), (200, 128, 17), (130, 1024, 100), (2048, 5632, 64),
+                                         (256, 2048, 300), (32000, 2048, 64), (6, 128, 1000)])
+def test_linear_tensor_core_shapes(rows, cols, n):
+    """tcgen05 linear on partial weight tiles (rows not a multiple of 128),
+    partial activation tiles, long K (split across clusters) and the
+    1.1B-shape matrices, against FP64."""
+    assert uses_tensor_cores(rows, cols, n)
+    q, s, x, packed = make(rows, cols, n, rows + 3 * cols + 7 * n)
+    y = ops.q6w_linear(torch.from_numpy(x).cuda(), packed, torch.from_numpy(s).cuda(), rows, cols).cpu().numpy()
+    worst = check(y, q, s, x, REL_TC, RMS_TC)
+    print(f"tensor-core linear {rows}x{cols} n={n}: max |err| / sum|w x| = {worst:.2e}")
 
 
 # One activation row at K a multiple of 512 takes the HBM-streaming kernel

@@ -986,6 +986,7 @@ static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st)
     case tc::TEPI_QKV: tc::tc_gemm_kernel<tc::TEPI_QKV><<<grid, tc::kThreads, smem, st>>>(a); break;
     case tc::TEPI_RESNORM: tc::tc_gemm_kernel<tc::TEPI_RESNORM><<<grid, tc::kThreads, smem, st>>>(a); break;
     case tc::TEPI_GLU: tc::tc_gemm_kernel<tc::TEPI_GLU><<<grid, tc::kThreads, smem, st>>>(a); break;
+    case tc::TEPI_STORE: tc::tc_gemm_kernel<tc::TEPI_STORE><<<grid, tc::kThreads, smem, st>>>(a); break;
     default: tc::tc_gemm_kernel<tc::TEPI_VOCAB><<<grid, tc::kThreads, smem, st>>>(a); break;
   }
   Q6W_LAUNCH_CHECK("tc_gemm_kernel");
@@ -1009,6 +1010,7 @@ static int32_t tc_set_attrs() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_RESNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_VOCAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tensor-core kernel attributes: %s", cudaGetErrorString(e));
   return Q6W_OK;
 }
@@ -1232,6 +1234,8 @@ static cudaError_t tcg_set_attrs() {
     e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_VOCAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tcg::tcg_kernel<tcg::GEPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   for (int l = 0; l < 4 && e == cudaSuccess; ++l) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(1 << l));
@@ -1299,7 +1303,7 @@ static int32_t weight_map(CUtensorMap* map, const uint8_t* q, int rows, int K, i
 
 static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st) {
   const bool glu = epi == tcg::GEPI_GLU;
-  const int wtiles = glu ? a.ms.n_pairs / (tcg::kWR / 2) : 2 * a.ms.n_pairs / tcg::kWR;
+  const int wtiles = tcg::weight_tiles(epi, a.ms);
   const int items = wtiles * ((a.n + tcg::kAR - 1) / tcg::kAR);
   const int nks = a.K / (64 * tcg::kG);  // K steps
   // split K over a cluster while the tiles alone would leave SMs idle and
@@ -1340,6 +1344,7 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
     case tcg::GEPI_QKV: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_QKV>, a, maps); break;
     case tcg::GEPI_RESID: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_RESID>, a, maps); break;
     case tcg::GEPI_GLU: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_GLU>, a, maps); break;
+    case tcg::GEPI_STORE: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_STORE>, a, maps); break;
     default: e = cudaLaunchKernelEx(&cfg, tcg::tcg_kernel<tcg::GEPI_VOCAB>, a, maps); break;
   }
   if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tcg_kernel launch: %s", cudaGetErrorString(e));
@@ -1347,9 +1352,12 @@ static int32_t tcg_launch(int epi, const tcg::GArgs& a, int sms, cudaStream_t st
 }
 
 static int32_t tcg_image(const float* x, int ldx, int n, int K, const float* g, float eps, uint8_t* img,
-                         cudaStream_t st) {
+                         cudaStream_t st, bool permuted = true) {
   if (K % 16 || K > tcg::kImgMaxK) return fail(Q6W_ERR_ARG, "image of K=%d unsupported", K);
-  tcg::image_kernel<<<n, tcg::kImgThreads, 0, st>>>(x, ldx, n, K, g, eps, img);
+  if (permuted)
+    tcg::image_kernel<true><<<n, tcg::kImgThreads, 0, st>>>(x, ldx, n, K, g, eps, img);
+  else
+    tcg::image_kernel<false><<<n, tcg::kImgThreads, 0, st>>>(x, ldx, n, K, g, eps, img);
   Q6W_LAUNCH_CHECK("image_kernel");
   return Q6W_OK;
 }
@@ -2013,4 +2021,97 @@ extern "C" int32_t q6w_gqa_attention(const float* queries, const float* keys, co
   }
   Q6W_LAUNCH_CHECK("attn_kernel");
   return Q6W_OK;
+}
+
+// ---- q6w_linear_ex: the batched linear on tensor cores ---------------------------
+//
+// For n >= 16 activation rows of a matrix whose width is a multiple of 128 (at
+// most 8192), x is written once as the three-part bf16 activation image (in
+// the caller's workspace) and a tcgen05 kernel runs with a plain store
+// epilogue: the persistent dim-128 kernel (tc.cuh; activations as the MMA's
+// 128-row M operand, weight tiles of 64-256 rows) when a weight tile with all
+// of K fits its staging area (K = 128 or 384 and the like), else the general
+// kernel (tcg.cuh; weights as M, split K across clusters).  Other shapes and
+// smaller n take q6w_linear's kernels.
+
+static bool linear_tc_ok(int64_t rows, int64_t cols, int64_t n) {
+  return n >= tcg_min_rows() && rows >= 2 && rows % 2 == 0 && cols % 128 == 0 && cols <= tcg::kImgMaxK &&
+         rows <= (1 << 24) && n <= (1 << 24);
+}
+
+// Per device: kernel attributes and the resident-cluster counts, set once.
+static int32_t linear_tc_setup() {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  Q6W_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(Q6W_ERR_ARG, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    int major = 0;
+    Q6W_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10) return fail(Q6W_ERR_ARG, "the tensor-core linear needs an sm_100 device");
+    const cudaError_t e = tcg_set_attrs();
+    if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tensor-core linear attributes: %s", cudaGetErrorString(e));
+    int32_t st = tc_set_attrs();
+    if (st) return st;
+    done[dev] = true;
+  }
+  return Q6W_OK;
+}
+
+extern "C" size_t q6w_linear_workspace_bytes(int64_t rows, int64_t cols, int64_t n) {
+  if (rows < 0 || cols < 0 || n < 0 || !linear_tc_ok(rows, cols, n)) return 0;
+  return 256 + tc::img_bytes(n, (int)cols);  // the error word (offset 0), then the activation image
+}
+
+extern "C" int32_t q6w_linear_ex(const uint8_t* packed, const float* scales, const float* x, float* y, int64_t rows,
+                                 int64_t cols, int64_t n, void* workspace, size_t workspace_bytes,
+                                 q6w_stream_t stream) {
+  clear_error();
+  if (rows < 0 || cols < 0 || n < 0) return fail(Q6W_ERR_ARG, "q6w_linear_ex: negative shape");
+  if (!workspace || !linear_tc_ok(rows, cols, n) || !aligned(packed, 16) || !aligned(scales, 4) ||
+      !aligned(x, 16) || !aligned(y, 8))
+    return q6w_linear(packed, scales, x, y, rows, cols, n, stream);
+  if (!packed || !scales || !x || !y) return fail(Q6W_ERR_ARG, "q6w_linear_ex: null pointer");
+  const size_t need = q6w_linear_workspace_bytes(rows, cols, n);
+  if (workspace_bytes < need)
+    return fail(Q6W_ERR_ARG, "q6w_linear_ex: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return fail(Q6W_ERR_ALIGN, "q6w_linear_ex: workspace must be 256-byte aligned");
+  int32_t st = linear_tc_setup();
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  // error word at offset 0 (q6w_workspace_status reads it), the image from byte 256
+  int32_t* err = static_cast<int32_t*>(workspace);
+  uint8_t* img = static_cast<uint8_t*>(workspace) + 256;
+  const int tile = tc::store_tile_rows(rows, cols);
+  if (tile && aligned(y, 16) && aligned(packed, 16) && aligned(scales, 16)) {
+    if ((st = tcg_image(x, (int)cols, (int)n, (int)cols, nullptr, 0.f, img, s, false))) return st;
+    tc::TcArgs t;
+    memset(&t, 0, sizeof(t));
+    t.a_img = img;
+    t.n = (int)n;
+    t.K = (int)cols;
+    t.q0 = packed;
+    t.s0 = scales;
+    t.end0 = t.end1 = (int32_t)rows;
+    t.N = tile;
+    t.n_tiles = (int32_t)(rows / tile);
+    t.ep.y = y;
+    t.ep.ldy = (int32_t)rows;
+    t.err = err;
+    return tc_launch(tc::TEPI_STORE, t, sm_count(), s);
+  }
+  if ((st = tcg_image(x, (int)cols, (int)n, (int)cols, nullptr, 0.f, img, s))) return st;
+  tcg::GArgs a;
+  memset(&a, 0, sizeof(a));
+  a.img = img;
+  a.n = (int)n;
+  a.K = (int)cols;
+  a.err = err;
+  a.ms = {packed, nullptr, nullptr, scales, nullptr, nullptr, (int32_t)rows, (int32_t)rows, (int32_t)cols, 0,
+          (int32_t)(rows / 2)};
+  a.ep.y = y;
+  a.ep.ldy = (int32_t)rows;
+  return tcg_launch(tcg::GEPI_STORE, a, sm_count(), s);
 }

@@ -186,7 +186,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 // ---- GEMM --------------------------------------------------------------------
 
-enum { TEPI_QKV = 0, TEPI_RESNORM = 1, TEPI_GLU = 2, TEPI_VOCAB = 3 };
+enum { TEPI_QKV = 0, TEPI_RESNORM = 1, TEPI_GLU = 2, TEPI_VOCAB = 3, TEPI_STORE = 4 };
+
+// Rows per N tile of the plain linear (TEPI_STORE) on this kernel, or 0 when
+// the shape does not fit it: K a multiple of 128, N in {256, 128, 64}
+// dividing rows, and N packed rows of K plus their scales within the
+// 37,376-byte staging area.
+__host__ __device__ inline int store_tile_rows(int64_t rows, int64_t K) {
+  if (K <= 0 || K % kKC) return 0;
+  for (int N = 256; N >= 64; N >>= 1)
+    if (rows % N == 0 && (int64_t)N * (K * 3 / 4 + 4) <= 128 * (288 + 4)) return N;
+  return 0;
+}
 
 struct TcArgs {
   const uint8_t* a_img;  // activation image [ceil(n/128) tiles][3][K]
@@ -443,6 +454,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
           }
       }
       if (live && bi >= 0) atomicMax(ep.keys + m, argmax_key(bv, bi));
+    } else if (EPI == TEPI_STORE) {
+      // the plain linear: y[m, nt N + c] = scale * D, 32 consecutive floats per load
+      const EpiArgs& ep = a.ep;
+      const int cb = half * (a.N >> 1), ce = cb + (a.N >> 1);
+      for (int c0 = cb; c0 < ce; c0 += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + c0, v);
+        if (!live) continue;
+        const int r0 = nt * a.N + c0;
+        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
+        float4* y = reinterpret_cast<float4*>(ep.y + m * ep.ldy + r0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 sc = s4[i];
+          y[i] = make_float4(__fmul_rn(v[4 * i], sc.x), __fmul_rn(v[4 * i + 1], sc.y),
+                             __fmul_rn(v[4 * i + 2], sc.z), __fmul_rn(v[4 * i + 3], sc.w));
+        }
+      }
     } else if (EPI == TEPI_QKV) {
       // Columns in two blocks through shared memory (sB): block 0 the q rows
       // [0, 128), block 1 the k and v rows [128, N).  E1 (this thread's row):

@@ -73,7 +73,16 @@ constexpr size_t kSmem = 1024 + (size_t)kS * kBT + (size_t)kP * kPT;
 // the partial tiles of every rank ([C][64 / C][128] floats) fit in the stage memory
 static_assert((size_t)kWR * kAR * 4 <= (size_t)kS * kBT, "partial tiles exceed the stages");
 
-enum { GEPI_QKV = 0, GEPI_RESID = 1, GEPI_GLU = 2, GEPI_VOCAB = 3 };
+enum { GEPI_QKV = 0, GEPI_RESID = 1, GEPI_GLU = 2, GEPI_VOCAB = 3, GEPI_STORE = 4 };
+
+// Weight tiles of a launch: whole 128-row tiles, except the plain linear
+// (GEPI_STORE), whose last tile may be partial (the TMA box reads zeros past
+// the last row and the epilogue stores only rows that exist).
+__host__ __device__ inline int weight_tiles(int epi, const MatSet& ms) {
+  if (epi == GEPI_GLU) return ms.n_pairs / (kWR / 2);
+  if (epi == GEPI_STORE) return (2 * ms.n_pairs + kWR - 1) / kWR;
+  return (2 * ms.n_pairs) / kWR;
+}
 
 struct GArgs {
   const uint8_t* img;   // activation image (tc.cuh layout) of K columns
@@ -168,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
   uint8_t* packed = smem + (size_t)kS * kBT;
   const int C = (int)cl.num_blocks(), c = (int)cl.block_rank();
   const int nks = a.K / (64 * kG);
-  const int wtiles = kGlu ? a.ms.n_pairs / (kWR / 2) : (2 * a.ms.n_pairs) / kWR;
+  const int wtiles = weight_tiles(EPI, a.ms);
   const int it = blockIdx.x / C;  // one item (weight tile, activation tile) per cluster
   const int wt = it % wtiles, at = it / wtiles;
   const int ks0 = c * (nks / C), nk = nks / C;  // this CTA's K steps
@@ -283,7 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
     if (tid < kWR) {
       int mi, r;
       weight_row(a.ms, kGlu, wt, tid, mi, r);
-      srow[tid] = __ldg(scale_ptr(a.ms, mi) + r);
+      // rows past the end of a partial GEPI_STORE tile have no scale
+      srow[tid] = (EPI != GEPI_STORE || wt * kWR + tid < 2 * a.ms.n_pairs) ? __ldg(scale_ptr(a.ms, mi) + r) : 0.0f;
     } else if (tid < kWR + kAR) {
       const int al = tid - kWR, m = at * kAR + al;
       const EpiArgs& ep = a.ep;
@@ -393,7 +403,11 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
       v0 = __fmul_rn(v0, s0);
       v1 = __fmul_rn(v1, s1);
       const int ml = c * SA + al, m = at * kAR + ml;
-      if (EPI == GEPI_GLU) {
+      if (EPI == GEPI_STORE) {
+        // the plain linear: y[m, rows] as row pairs, 64 consecutive floats per warp
+        if (m < a.n && vrow < 2 * a.ms.n_pairs)
+          *reinterpret_cast<float2*>(ep.y + (int64_t)m * ep.ldy + vrow) = make_float2(v0, v1);
+      } else if (EPI == GEPI_GLU) {
         if (m < a.n) ep.y[(int64_t)m * ep.ldy + wt * (kWR / 2) + pp] = swiglu(v0, v1);
       } else if (EPI == GEPI_RESID) {
         // the only writer of this element: one rounded add onto the residual
@@ -465,6 +479,9 @@ constexpr int kImgThreads = 256;
 constexpr int kImgGroups = 2;
 constexpr int kImgMaxK = 16 * kImgThreads * kImgGroups;
 
+// PERM = false writes the columns in natural order: the image tc.cuh's
+// kernel reads (its weight expansion keeps the natural K order).
+template <bool PERM = true>
 __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restrict__ x, int ldx, int n, int K,
                                                             const float* __restrict__ g, float eps,
                                                             uint8_t* __restrict__ img) {
@@ -511,9 +528,14 @@ __global__ void __launch_bounds__(kImgThreads) image_kernel(const float* __restr
 #pragma unroll
   for (int c = 0; c < kImgGroups; ++c) {
     const int k0 = 16 * (tid + kImgThreads * c);
-    if (k0 < K) {
+    if (k0 < K && PERM) {
       const float lo[8] = {v[c][0], v[c][4], v[c][8], v[c][12], v[c][3], v[c][7], v[c][11], v[c][15]};
       const float hi[8] = {v[c][2], v[c][6], v[c][10], v[c][14], v[c][1], v[c][5], v[c][9], v[c][13]};
+      tc::img_store8(img, row, k0, K, lo);
+      tc::img_store8(img, row, k0 + 8, K, hi);
+    } else if (k0 < K) {
+      const float lo[8] = {v[c][0], v[c][1], v[c][2], v[c][3], v[c][4], v[c][5], v[c][6], v[c][7]};
+      const float hi[8] = {v[c][8], v[c][9], v[c][10], v[c][11], v[c][12], v[c][13], v[c][14], v[c][15]};
       tc::img_store8(img, row, k0, K, lo);
       tc::img_store8(img, row, k0 + 8, K, hi);
     }

@@ -26,7 +26,7 @@ EXPORTS = (
     "q6w_model_create", "q6w_model_destroy", "q6w_workspace_bytes", "q6w_step",
     "q6w_forward_batch", "q6w_generate_greedy", "q6w_workspace_status", "q6w_linear_argmax",
     "q6w_rmsnorm", "q6w_gqa_attention", "q6w_linear_argmax_noalloc", "q6w_prefill_workspace_bytes",
-    "q6w_prefill", "q6w_quantize_rows",
+    "q6w_prefill", "q6w_quantize_rows", "q6w_linear_workspace_bytes", "q6w_linear_ex",
 )
 
 
@@ -79,6 +79,9 @@ def _declare(lib):
         "q6w_unpack": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, S]),
         "q6w_dequant": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, S]),
         "q6w_quantize_rows": (c_int32, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, S]),
+        "q6w_linear_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+        "q6w_linear_ex": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
+                                    c_size_t, S]),
         "q6w_linear": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, S]),
         "q6w_model_create": (c_int32, [POINTER(ModelDesc), POINTER(c_void_p)]),
         "q6w_model_destroy": (None, [c_void_p]),

@@ -90,16 +90,49 @@ def quantize_rows(tensor, device="cuda"):
     return packed, scales, {"max_abs_error": st[0], "mean_abs_error": st[1], "rmse": st[2]}
 
 
-def q6w_linear(x, packed, scales, rows, columns):
-    """``x @ dequant(W).T`` for x [..., columns] FP32 on the GPU -> [..., rows]."""
+_LINEAR_WS = {}  # device index -> cached workspace of the tensor-core linear
+
+
+def _linear_workspace(device, nbytes):
+    buf = _LINEAR_WS.get(device.index)
+    if buf is None or buf.numel() < nbytes:
+        raw = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+        off = (-raw.data_ptr()) % 256
+        buf = raw[off: off + nbytes]
+        _LINEAR_WS[device.index] = buf
+    return buf
+
+
+def linear_workspace_bytes(rows, columns, n):
+    """Workspace the tensor-core linear needs for this shape (0: FP32 kernels)."""
+    return int(_lib.load().q6w_linear_workspace_bytes(rows, columns, n))
+
+
+def q6w_linear(x, packed, scales, rows, columns, tensor_cores=True):
+    """``x @ dequant(W).T`` for x [..., columns] FP32 on the GPU -> [..., rows].
+
+    The ``nn.Linear`` of the cached step (torch_benchmark.py:105-107, 121,
+    123, 125).  Batches of 16 or more rows whose width is a multiple of 128
+    run on the tcgen05 tensor cores (q6w_linear_ex, a cached workspace per
+    device; agreement with FP64 within 1e-4 * sum|w x| per element); other
+    shapes, and ``tensor_cores=False``, run the FP32 kernels (1e-5).
+    """
     if x.dtype != torch.float32 or x.shape[-1] != columns:
         raise ValueError("x must be float32 with last dimension == columns")
     xs = x.reshape(-1, columns).contiguous()
-    y = torch.empty((xs.shape[0], rows), dtype=torch.float32, device=x.device)
+    n = xs.shape[0]
+    y = torch.empty((n, rows), dtype=torch.float32, device=x.device)
     lib = _lib.load()
+    need = linear_workspace_bytes(rows, columns, n) if tensor_cores else 0
     with torch.cuda.device(x.device):
-        _lib.check(lib.q6w_linear(packed.data_ptr(), scales.data_ptr(), xs.data_ptr(), y.data_ptr(), rows,
-                                  columns, xs.shape[0], _lib.stream_handle()), "q6w_linear")
+        if need:
+            ws = _linear_workspace(x.device, need)
+            _lib.check(lib.q6w_linear_ex(packed.data_ptr(), scales.data_ptr(), xs.data_ptr(), y.data_ptr(), rows,
+                                         columns, n, ws.data_ptr(), ws.numel(), _lib.stream_handle()),
+                       "q6w_linear_ex")
+        else:
+            _lib.check(lib.q6w_linear(packed.data_ptr(), scales.data_ptr(), xs.data_ptr(), y.data_ptr(), rows,
+                                      columns, n, _lib.stream_handle()), "q6w_linear")
     return y.reshape(*x.shape[:-1], rows)
 
 
