@@ -274,6 +274,47 @@ typedef struct q6w_greedy_args {
 Q6W_API int32_t q6w_generate_greedy(q6w_model* model, const q6w_greedy_args* args, void* workspace,
                             size_t workspace_bytes, q6w_stream_t stream);
 
+/* Sampling and logit shaping of torch_benchmark.generate
+ * (benchmarks/torch_benchmark.py:133-230, applied as in :272-286).  Values
+ * the reference applies to FP32 logits (temperature, repetition_penalty,
+ * stop_token_bias) act as their FP32 roundings, as torch applies a Python
+ * float to a float32 tensor; top_p is compared in FP64 as in the reference. */
+typedef struct q6w_sample_args {
+  float temperature;             /* 0: the first maximum of the shaped logits (greedy) */
+  double top_p;                  /* nucleus mass; <= 0 or >= 1: scan over every token */
+  float repetition_penalty;      /* 1: off; else logits of generated tokens: l < 0 ? l * p : l / p */
+  int32_t no_repeat_ngram_size;  /* 0: off */
+  float stop_token_bias;         /* added to the stop ids' logits from decode index stop_token_bias_after on */
+  int32_t stop_token_bias_after; /* the reference's default is min_new_tokens */
+  const uint64_t* seeds;         /* [n_seqs] device array: XorShift64 seed of each request (temperature > 0) */
+} q6w_sample_args;
+
+/* q6w_generate_greedy with the reference's sampler: with `sampling` NULL (or
+ * temperature 0 and no shaping) this is the greedy loop; otherwise every
+ * step's logits row goes through the repetition penalty, n-gram blocking,
+ * stop-id masking (before min_new_tokens) or bias (from
+ * stop_token_bias_after on), and temperature / top-p sampling with one
+ * XorShift64 generator per request seeded from `seeds`, all on the device
+ * in the same CUDA graph step.  The workspace is q6w_workspace_bytes (it
+ * includes the sampler's [n, vocab] logits and generator states).  A picked
+ * stop id ends the request (not appended), as in generate. */
+Q6W_API int32_t q6w_generate(q6w_model* model, const q6w_greedy_args* args, const q6w_sample_args* sampling,
+                             void* workspace, size_t workspace_bytes, q6w_stream_t stream);
+
+/* The sampler alone, on n rows of logits (row i at logits + i * ld, vocab
+ * columns; not modified): replaces the reference's per-step host code of
+ * generate (:272-285) for callers that compute logits themselves.
+ * history [n, history_ld] holds each row's generated tokens (history_len[i]
+ * of them, which is also the decode index for stop masking and bias);
+ * rng_state [n] holds each row's XorShift64 state (a new generator's state
+ * is its seed) and is advanced when a coin is drawn; stop_ids is a host
+ * array of n_stop (<= 8) ids.  tokens [n] receives the picks.  Device
+ * arrays unless marked host; vocab <= 32768. */
+Q6W_API int32_t q6w_sample(const float* logits, int64_t ld, int32_t n, int32_t vocab, const int32_t* history,
+                           int64_t history_ld, const int32_t* history_len, uint64_t* rng_state,
+                           const q6w_sample_args* sampling, const int32_t* stop_ids, int32_t n_stop,
+                           int32_t min_new_tokens, int32_t* tokens, q6w_stream_t stream);
+
 /* Synchronise `stream` and report device-side input errors recorded in the
  * workspace since the last call (then clear them): Q6W_OK or Q6W_ERR_DEVICE. */
 Q6W_API int32_t q6w_workspace_status(void* workspace, q6w_stream_t stream);

@@ -32,6 +32,16 @@ It imports the reference's own ``quantization/q6w_format.py`` and
   story-opening request (prompt ids from the shipped tokenizer), 128 greedy
   tokens with min_new_tokens 4 and stop ids {BOS, EOS}.  The artifact itself
   is not copied here.
+
+``--sampling`` writes only the two fixtures below (the others stay as recorded):
+
+* ``sampling.json`` -- the reference's ``generate`` at temperature > 0 and
+  with its logit processors (repetition penalty, n-gram blocking, stop-id
+  masking and bias) on the tiny synthetic model and the golden prompt, six
+  settings, 64 tokens each;
+* ``fp16_kv.json`` / ``fp16_kv_logits.npz`` -- the reference's FP16-KV
+  wrapper (quantization/compare_kv_cache.py) on the same request: 128 greedy
+  tokens and the logits of the last prompt step and four decode steps.
 """
 
 import hashlib
@@ -181,6 +191,62 @@ def shipped_request():
             "margins": run["margins"], "torch": torch.__version__}
 
 
+SAMPLING_CASES = [
+    {"temperature": 0.8, "top_p": 0.9, "seed": 1},
+    {"temperature": 1.0, "top_p": 1.0, "seed": 7},
+    {"temperature": 0.7, "top_p": 0.95, "seed": 3, "repetition_penalty": 1.3, "no_repeat_ngram_size": 3},
+    {"temperature": 0.9, "top_p": 0.9, "seed": 11, "min_new_tokens": 4, "stop_token_bias": 8.0,
+     "stop_token_bias_after": 8, "stop": True},
+    {"temperature": 0.0, "top_p": 0.9, "seed": 1, "repetition_penalty": 1.2, "no_repeat_ngram_size": 2},
+    {"temperature": 1.2, "top_p": 0.5, "seed": 42, "no_repeat_ngram_size": 1},
+]
+
+
+def sampling_requests(tmp):
+    """The reference's own ``generate`` at temperature > 0 and with its logit
+    processors, on the tiny synthetic model and the golden 20-token prompt."""
+    b, m = tmp / "tiny.bin", tmp / "tiny.json"
+    fmt.write_synthetic(fmt.TINY_ARGS, TINY_SEED, b, m)
+    model, _ = load_reference_model(b, m)
+    prompt = torch.randint(3, 4096, (20,), generator=torch.Generator().manual_seed(PROMPT_SEED)).tolist()
+    cases = []
+    stop_id = None
+    for case in SAMPLING_CASES:
+        kw = {k: v for k, v in case.items() if k != "stop"}
+        if case.get("stop"):
+            kw["stop_token"] = {stop_id}
+        with torch.inference_mode():
+            gen, _, _, stopped, reason = ref_tb.generate(model, prompt, 64, torch.device("cpu"), **kw)
+        if stop_id is None:
+            stop_id = gen[12]  # a token the model samples, for the stop case
+        cases.append({"kwargs": {k: (sorted(v) if isinstance(v, set) else v) for k, v in kw.items()},
+                      "new_tokens": 64, "generated": gen, "stopped": stopped, "stop_reason": reason})
+    return {"seed": TINY_SEED, "prompt": prompt, "cases": cases, "torch": torch.__version__}
+
+
+def fp16_kv_request(tmp):
+    """The reference's FP16-KV wrapper (quantization/compare_kv_cache.py:15-72)
+    on the tiny synthetic model: the golden prompt + 128 greedy tokens, and
+    the logits of the last prompt step and the first decode steps."""
+    sys.path.insert(0, str(REF / "quantization"))
+    import compare_kv_cache as ref_kv
+
+    b, m = tmp / "tiny16.bin", tmp / "tiny16.json"
+    fmt.write_synthetic(fmt.TINY_ARGS, TINY_SEED, b, m)
+    model, _ = load_reference_model(b, m)
+    fp16 = ref_kv.FP16KVTransformer(model)
+    prompt = torch.randint(3, 4096, (20,), generator=torch.Generator().manual_seed(PROMPT_SEED)).tolist()
+    with torch.inference_mode():
+        gen, _, _, _, _ = ref_tb.generate(fp16, prompt, 128, torch.device("cpu"))
+        k, v = fp16.new_cache(torch.device("cpu"))
+        rows = []
+        for pos, tok in enumerate(prompt + gen[:4]):
+            lg = fp16.step(tok, pos, k, v)
+            if pos >= len(prompt) - 1:
+                rows.append(lg.clone())
+    return {"prompt": prompt, "generated": gen}, torch.stack(rows).numpy()
+
+
 SHIPPED = "tinyllamas_zh_story_q6w_qat_lr1e6"
 
 
@@ -199,6 +265,14 @@ def main():
         copy_shipped()
         return
     torch.set_num_threads(1)
+    if "--sampling" in sys.argv:  # only the sampling and FP16-KV fixtures (the others stay as recorded)
+        with tempfile.TemporaryDirectory() as d:
+            (HERE / "sampling.json").write_text(json.dumps(sampling_requests(Path(d)), indent=1) + "\n")
+            doc, rows = fp16_kv_request(Path(d))
+        (HERE / "fp16_kv.json").write_text(json.dumps(doc, indent=1) + "\n")
+        np.savez_compressed(HERE / "fp16_kv_logits.npz", rows=rows)
+        print("sampling and FP16-KV fixtures written to", HERE)
+        return
     (HERE / "codec.json").write_text(json.dumps(codec_vectors(), indent=1) + "\n")
     with tempfile.TemporaryDirectory() as d:
         doc, logits = tiny_request(Path(d))

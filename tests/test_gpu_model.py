@@ -77,8 +77,8 @@ def test_generate_matches_reference_signature_errors(tiny):
     cuda, _ = tiny
     with pytest.raises(ValueError):
         generate(cuda, [5, 6], 4, cuda.device, min_new_tokens=5)
-    with pytest.raises(NotImplementedError):
-        generate(cuda, [5, 6], 4, cuda.device, temperature=0.7)
+    with pytest.raises(ValueError):
+        generate(cuda, [5, 6], 4, cuda.device, temperature=0.7, repetition_penalty=-1.0)
     with pytest.raises(ValueError):
         cuda.generate_greedy([[1] * 250], 10)  # exceeds the 256-position context
 

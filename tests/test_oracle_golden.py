@@ -87,3 +87,44 @@ def test_batch_scorer_agrees_with_step(tiny_files, golden_tiny):
     bad = [list(o["sampled"]) for o in outs]
     bad[1][3] = (bad[1][3] + 1) % 4096
     assert sc.verify_greedy(prompts, bad, 12)["failures"]
+
+
+@pytest.fixture(scope="module")
+def golden_sampling():
+    import json
+
+    from conftest import GOLDEN
+
+    return json.loads((GOLDEN / "sampling.json").read_text())
+
+
+def test_oracle_sampler_reproduces_reference_streams(tiny_files, golden_sampling):
+    """XorShift64, temperature / top-p sampling and the repetition, n-gram and
+    stop-bias processors of the oracle give the reference generate()'s tokens."""
+    from oracle.sampler import sampled_request
+
+    torch.set_num_threads(1)
+    orc = OracleModel.from_q6w(*tiny_files)
+    for case in golden_sampling["cases"]:
+        kw = dict(case["kwargs"])
+        if "stop_token" in kw:
+            kw["stop_token"] = set(kw["stop_token"])
+        got = sampled_request(orc, golden_sampling["prompt"], case["new_tokens"], **kw)
+        assert got["generated"] == case["generated"], kw
+        assert got["stopped"] == case["stopped"] and got["stop_reason"] == case["stop_reason"]
+
+
+def test_xorshift_known_values():
+    """The reference generator's first draws for seed 1 (torch_benchmark.py:133-144), restated by hand."""
+    from oracle.sampler import XorShift64
+
+    mask = (1 << 64) - 1
+    s = 1
+    want = []
+    for _ in range(3):
+        s ^= s >> 12
+        s ^= (s << 25) & mask
+        s ^= s >> 27
+        want.append((((s * 0x2545F4914F6CDD1D) & mask) >> 40) / 16777216.0)
+    r = XorShift64(1)
+    assert [r.random_f32() for _ in range(3)] == want

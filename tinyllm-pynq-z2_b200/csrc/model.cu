@@ -26,6 +26,7 @@
 
 #include "b1.cuh"
 #include "launch.cuh"
+#include "sample.cuh"
 #include "tc.cuh"
 #include "tcg.cuh"
 
@@ -49,12 +50,16 @@ struct Work {
   uint8_t* att_img;
   uint8_t* hs_img;
   const int32_t* seq;  // cache row of each activation row (prefill: rows are tokens); null: row i
+  float* logits;       // sampling: the step's logits [N, vocab] (null unless laid out for sampling)
+  unsigned long long* rng;  // sampling: XorShift64 state per sequence
 };
 
 struct GraphKey {
   q6w_greedy_args a;
   int32_t stop[kMaxStop];
   void* ws;
+  int32_t sampler;          // the step graph runs the sampler kernel
+  smp::Params sp;
 };
 
 }  // namespace q6w
@@ -84,7 +89,10 @@ static size_t carve(char*& p, size_t bytes) {
   return off;
 }
 
-static size_t layout(const q6w_model* M, int N, char* base, Work* w) {
+// Workspace of N sequences.  With `sample`, the sampler's regions (the step
+// logits and the generator states) follow the rest, so every other offset is
+// the same with or without them.
+static size_t layout(const q6w_model* M, int N, char* base, Work* w, bool sample = false) {
   const auto& d = M->d;
   char* p = base;
   Work t;
@@ -107,6 +115,12 @@ static size_t layout(const q6w_model* M, int N, char* base, Work* w) {
     t.xs_img = t.att_img = t.hs_img = nullptr;
   }
   t.seq = nullptr;
+  t.logits = nullptr;
+  t.rng = nullptr;
+  if (sample) {
+    t.logits = (float*)carve(p, sizeof(float) * (size_t)N * d.vocab_size);
+    t.rng = (unsigned long long*)carve(p, 8 * (size_t)N);
+  }
   if (w) *w = t;
   return (size_t)(p - base);
 }
@@ -129,8 +143,9 @@ __global__ void init_batch_kernel(int n, const int32_t* __restrict__ tokens,
 __global__ void init_greedy_kernel(int n, const int32_t* __restrict__ prompts,
                                    const int32_t* __restrict__ lens, int32_t stride,
                                    int32_t max_len, Work w, int32_t* n_sampled,
-                                   int32_t* stop_reason) {
+                                   int32_t* stop_reason, const unsigned long long* __restrict__ seeds) {
   for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n; b += gridDim.x * blockDim.x) {
+    if (w.rng) w.rng[b] = seeds ? seeds[b] : 0ull;  // XorShift64(seed): the state is the seed
     const int32_t L = lens[b];
     const bool ok = L >= 1 && L <= max_len;
     w.tok[b] = ok ? prompts[(int64_t)b * stride] : 0;
@@ -1641,16 +1656,60 @@ extern "C" void q6w_model_destroy(q6w_model* M) {
 
 extern "C" size_t q6w_workspace_bytes(const q6w_model* M, int32_t max_seqs) {
   if (!M || max_seqs < 0) return 0;
-  return layout(M, max_seqs, nullptr, nullptr);
+  return layout(M, max_seqs, nullptr, nullptr, true);
 }
 
-static int32_t check_ws(const q6w_model* M, int n, void* ws, size_t bytes, Work* w) {
+static int32_t check_ws(const q6w_model* M, int n, void* ws, size_t bytes, Work* w, bool sample = false) {
   if (!ws) return fail(Q6W_ERR_ARG, "null workspace");
   if (!aligned(ws, 256)) return fail(Q6W_ERR_ALIGN, "workspace must be 256-byte aligned");
-  if (layout(M, n, nullptr, nullptr) > bytes)
-    return fail(Q6W_ERR_ARG, "workspace of %zu bytes too small for %d sequences (%zu needed)", bytes, n,
-                layout(M, n, nullptr, nullptr));
-  layout(M, n, (char*)ws, w);
+  const size_t need = layout(M, n, nullptr, nullptr, sample);
+  if (need > bytes)
+    return fail(Q6W_ERR_ARG, "workspace of %zu bytes too small for %d sequences (%zu needed)", bytes, n, need);
+  layout(M, n, (char*)ws, w, sample);
+  return Q6W_OK;
+}
+
+// Sampler parameters from the C struct (validated as torch_benchmark.generate
+// validates them, :246-255); the Python-float values rounded to FP32 where
+// the reference applies them to FP32 tensors.
+static int32_t make_sample_params(const q6w_sample_args* s, int vocab, const StopSet& stop, smp::Params* p) {
+  memset(p, 0, sizeof(*p));
+  if (!(s->temperature >= 0.0f) || !isfinite(s->temperature))
+    return fail(Q6W_ERR_ARG, "temperature must be finite and >= 0");
+  if (!(s->repetition_penalty > 0.0f) || !isfinite(s->stop_token_bias) || s->stop_token_bias_after < 0 ||
+      s->no_repeat_ngram_size < 0)
+    return fail(Q6W_ERR_ARG, "repetition_penalty must be positive, stop_token_bias finite, min_new_tokens within "
+                             "the limit, and bias/ngram settings nonnegative");
+  if (vocab > smp::kMaxVocab) return fail(Q6W_ERR_ARG, "sampling supports vocabularies up to %d", smp::kMaxVocab);
+  p->temperature = s->temperature;
+  p->repetition_penalty = s->repetition_penalty;
+  p->stop_bias = s->stop_token_bias;
+  p->top_p = s->top_p;
+  p->nucleus = s->top_p > 0.0 && s->top_p < 1.0;
+  p->cutoff = (float)((1.0 - s->top_p) / (double)(vocab - 1));
+  p->ngram = s->no_repeat_ngram_size;
+  p->bias_after = s->stop_token_bias_after;
+  p->min_new = stop.min_new;
+  p->n_stop = stop.n;
+  for (int i = 0; i < kMaxStop; ++i) p->stop_ids[i] = stop.ids[i];
+  return Q6W_OK;
+}
+
+// Whether the step needs the sampler (anything but a plain greedy pick).
+static bool needs_sampler(const smp::Params& p) {
+  return p.temperature != 0.0f || p.repetition_penalty != 1.0f || p.ngram != 0 || (p.n_stop && p.stop_bias != 0.0f);
+}
+
+static int32_t sample_attr(int vocab) {
+  static std::mutex mu;
+  static size_t set_to[64] = {0};
+  int dev = 0;
+  Q6W_CUDA_TRY(cudaGetDevice(&dev));
+  const size_t need = smp::smem_bytes(vocab);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && set_to[dev] >= need) return Q6W_OK;
+  Q6W_CUDA_TRY(cudaFuncSetAttribute(smp::sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need));
+  if (dev >= 0 && dev < 64) set_to[dev] = need;
   return Q6W_OK;
 }
 
@@ -1718,7 +1777,7 @@ extern "C" int32_t q6w_forward_batch(const q6w_model* M, int32_t n, const int32_
 }
 
 static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& w,
-                            const StopSet& stop) {
+                            const StopSet& stop, const smp::Params* sp) {
   if (!M->cap_stream) Q6W_CUDA_TRY(cudaStreamCreateWithFlags(&M->cap_stream, cudaStreamNonBlocking));
   if (M->exec) {
     cudaGraphExecDestroy(M->exec);
@@ -1731,10 +1790,32 @@ static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& 
   v.step_logits = a->step_logits;
   v.new_tokens = a->new_tokens;
   v.min_new = stop.min_new;
-  v.n_stop = stop.n;
+  v.n_stop = sp ? 0 : stop.n;  // with the sampler, the stop ids are handled there
   for (int i = 0; i < kMaxStop; ++i) v.stop_ids[i] = stop.ids[i];
+  if (sp) {
+    v.y = w.logits;  // the raw logits row of every sequence, for the sampler
+    v.ldy = M->d.vocab_size;
+  }
   int32_t st = enqueue_step(M, a->n_seqs, w, a->k_cache, a->v_cache, a->cache_seq_stride, v,
                             M->cap_stream);
+  if (st == Q6W_OK && sp) {
+    smp::Args sa;
+    memset(&sa, 0, sizeof(sa));
+    sa.logits = w.logits;
+    sa.ld = M->d.vocab_size;
+    sa.vocab = M->d.vocab_size;
+    sa.hist = a->sampled;
+    sa.hist_ld = a->new_tokens;
+    sa.hist_len = w.gen;
+    sa.rng = w.rng;
+    sa.keys = w.keys;
+    sa.flags = w.flags;
+    sa.pos = w.pos;
+    sa.plen = w.plen;
+    sa.p = *sp;
+    smp::sample_kernel<<<a->n_seqs, smp::kThreads, smp::smem_bytes(M->d.vocab_size), M->cap_stream>>>(sa);
+    if (cudaGetLastError() != cudaSuccess) st = fail(Q6W_ERR_CUDA, "sample_kernel launch failed");
+  }
   if (st == Q6W_OK) {
     advance_kernel<<<grid_for(a->n_seqs, 256), 256, 0, M->cap_stream>>>(
         a->n_seqs, w, a->prompts, a->prompt_stride, a->new_tokens, stop, a->sampled, a->n_sampled,
@@ -1845,8 +1926,8 @@ extern "C" int32_t q6w_prefill(const q6w_model* M, int32_t n_prompts, const int3
   return Q6W_OK;
 }
 
-extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, void* workspace,
-                                       size_t workspace_bytes, q6w_stream_t stream) {
+extern "C" int32_t q6w_generate(q6w_model* M, const q6w_greedy_args* a, const q6w_sample_args* sampling,
+                                void* workspace, size_t workspace_bytes, q6w_stream_t stream) {
   clear_error();
   if (!M || !a) return fail(Q6W_ERR_ARG, "null argument");
   const int n = a->n_seqs;
@@ -1873,15 +1954,27 @@ extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, v
       return fail(Q6W_ERR_RANGE, "stop id %d outside the vocabulary", a->stop_ids[i]);
     stop.ids[i] = a->stop_ids[i];
   }
+  smp::Params sp;
+  bool sampler = false;
+  int32_t st;
+  if (sampling) {
+    if ((st = make_sample_params(sampling, M->d.vocab_size, stop, &sp))) return st;
+    sampler = needs_sampler(sp);
+    if (sampler && sp.temperature != 0.0f && !sampling->seeds)
+      return fail(Q6W_ERR_ARG, "sampling at temperature > 0 needs one seed per sequence");
+    if (sampler && a->new_tokens > smp::kMaxHistory)
+      return fail(Q6W_ERR_ARG, "sampling supports at most %d new tokens per request", smp::kMaxHistory);
+    if (sampler && (st = sample_attr(M->d.vocab_size))) return st;
+  }
   Work w;
-  int32_t st = check_ws(M, n, workspace, workspace_bytes, &w);
+  st = check_ws(M, n, workspace, workspace_bytes, &w, sampler);
   if (st) return st;
   if ((st = check_cache(M, a->k_cache, a->v_cache, a->cache_seq_stride, n))) return st;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != M->device) return fail(Q6W_ERR_ARG, "model was created on device %d, current is %d", M->device, dev);
 
-  if (n == 1 && M->use_b1) {  // one request: the cluster kernel runs the whole loop
+  if (n == 1 && M->use_b1 && !sampler) {  // one greedy request: the cluster kernel runs the whole loop
     cudaStream_t s = (cudaStream_t)stream;
     b1::Args ba;
     b1_fill(M, ba);
@@ -1924,14 +2017,18 @@ extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, v
   key.a.prefill_event = nullptr;
   memcpy(key.stop, stop.ids, sizeof(key.stop));
   key.ws = workspace;
+  key.sampler = sampler;
+  if (sampler) key.sp = sp;
   if (!M->exec || !M->have_key || memcmp(&key, &M->key, sizeof(key)) != 0) {
-    if ((st = capture_step(M, a, w, stop))) return st;
+    if ((st = capture_step(M, a, w, stop, sampler ? &sp : nullptr))) return st;
     M->key = key;
     M->have_key = true;
   }
   cudaStream_t s = (cudaStream_t)stream;
   init_greedy_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, a->prompts, a->prompt_lens, a->prompt_stride,
-                                                      a->max_prompt_len, w, a->n_sampled, a->stop_reason);
+                                                      a->max_prompt_len, w, a->n_sampled, a->stop_reason,
+                                                      sampler ? reinterpret_cast<const unsigned long long*>(
+                                                                    sampling->seeds) : nullptr);
   Q6W_LAUNCH_CHECK("init_greedy_kernel");
   const int steps = a->max_prompt_len + a->new_tokens - 1;
   for (int i = 0; i < steps; ++i) {
@@ -1939,6 +2036,47 @@ extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, v
     if (i + 1 == a->max_prompt_len && a->prefill_event)
       Q6W_CUDA_TRY(cudaEventRecord((cudaEvent_t)a->prefill_event, s));
   }
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_generate_greedy(q6w_model* M, const q6w_greedy_args* a, void* workspace,
+                                       size_t workspace_bytes, q6w_stream_t stream) {
+  return q6w_generate(M, a, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int32_t q6w_sample(const float* logits, int64_t ld, int32_t n, int32_t vocab, const int32_t* history,
+                              int64_t history_ld, const int32_t* history_len, uint64_t* rng_state,
+                              const q6w_sample_args* sampling, const int32_t* stop_ids, int32_t n_stop,
+                              int32_t min_new_tokens, int32_t* tokens, q6w_stream_t stream) {
+  clear_error();
+  if (n < 0 || vocab < 2 || ld < vocab || history_ld < 0) return fail(Q6W_ERR_ARG, "q6w_sample: bad shape");
+  if (!sampling) return fail(Q6W_ERR_ARG, "q6w_sample: null sampling arguments");
+  if (n_stop < 0 || n_stop > kMaxStop || (n_stop && !stop_ids)) return fail(Q6W_ERR_ARG, "n_stop must be in [0, %d]", kMaxStop);
+  if (n == 0) return Q6W_OK;
+  if (!logits || !history_len || !rng_state || !tokens || (history_ld > 0 && !history))
+    return fail(Q6W_ERR_ARG, "q6w_sample: null pointer");
+  StopSet stop;
+  memset(&stop, 0, sizeof(stop));
+  stop.n = n_stop;
+  stop.min_new = min_new_tokens;
+  for (int i = 0; i < n_stop; ++i) stop.ids[i] = stop_ids[i];
+  smp::Params sp;
+  int32_t st = make_sample_params(sampling, vocab, stop, &sp);
+  if (st) return st;
+  if ((st = sample_attr(vocab))) return st;
+  smp::Args sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.logits = logits;
+  sa.ld = ld;
+  sa.vocab = vocab;
+  sa.hist = history;
+  sa.hist_ld = history_ld;
+  sa.hist_len = history_len;
+  sa.rng = reinterpret_cast<unsigned long long*>(rng_state);
+  sa.tokens = tokens;
+  sa.p = sp;
+  smp::sample_kernel<<<n, smp::kThreads, smp::smem_bytes(vocab), (cudaStream_t)stream>>>(sa);
+  Q6W_LAUNCH_CHECK("sample_kernel");
   return Q6W_OK;
 }
 

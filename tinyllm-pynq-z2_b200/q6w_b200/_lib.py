@@ -26,7 +26,8 @@ EXPORTS = (
     "q6w_model_create", "q6w_model_destroy", "q6w_workspace_bytes", "q6w_step",
     "q6w_forward_batch", "q6w_generate_greedy", "q6w_workspace_status", "q6w_linear_argmax",
     "q6w_rmsnorm", "q6w_gqa_attention", "q6w_linear_argmax_noalloc", "q6w_prefill_workspace_bytes",
-    "q6w_prefill", "q6w_quantize_rows", "q6w_linear_workspace_bytes", "q6w_linear_ex",
+    "q6w_prefill", "q6w_quantize_rows", "q6w_linear_workspace_bytes", "q6w_linear_ex", "q6w_generate",
+    "q6w_sample",
 )
 
 
@@ -56,6 +57,12 @@ class ModelDesc(ctypes.Structure):
                 ("vocab_size", c_int32), ("hidden_dim", c_int32), ("max_seq_len", c_int32),
                 ("norm_eps", c_float), ("tok_embeddings", QMat), ("norm", c_void_p),
                 ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("layers", POINTER(LayerWeights))]
+
+
+class SampleArgs(ctypes.Structure):
+    _fields_ = [("temperature", c_float), ("top_p", ctypes.c_double), ("repetition_penalty", c_float),
+                ("no_repeat_ngram_size", c_int32), ("stop_token_bias", c_float), ("stop_token_bias_after", c_int32),
+                ("seeds", c_void_p)]
 
 
 class GreedyArgs(ctypes.Structure):
@@ -90,6 +97,9 @@ def _declare(lib):
         "q6w_forward_batch": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                         c_void_p, c_void_p, c_void_p, c_size_t, S]),
         "q6w_generate_greedy": (c_int32, [c_void_p, POINTER(GreedyArgs), c_void_p, c_size_t, S]),
+        "q6w_generate": (c_int32, [c_void_p, POINTER(GreedyArgs), POINTER(SampleArgs), c_void_p, c_size_t, S]),
+        "q6w_sample": (c_int32, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                                 POINTER(SampleArgs), POINTER(c_int32), c_int32, c_int32, c_void_p, S]),
         "q6w_workspace_status": (c_int32, [c_void_p, S]),
         "q6w_linear_argmax": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                         c_int64, c_int64, c_int64, S]),

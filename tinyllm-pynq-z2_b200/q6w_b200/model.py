@@ -280,12 +280,15 @@ class Q6WCudaTransformer:
         return lg, caches
 
     def generate_greedy_device(self, prompts, prompt_lens, max_prompt_len, new_tokens, stop_ids=(),
-                               min_new_tokens=0, caches=None, keep_logits=False, prefill_event=None):
-        """Device-resident greedy generation (no host sync inside).
+                               min_new_tokens=0, caches=None, keep_logits=False, prefill_event=None, sampling=None):
+        """Device-resident generation (no host sync inside).
 
         ``prompts``: device int32 [n, stride]; ``prompt_lens``: device int32 [n].
-        Returns device tensors (sampled [n, new_tokens], n_sampled [n],
-        stop_reason [n], step_logits or None, caches).  Does not synchronise.
+        ``sampling``: None (greedy) or a ``sampling_args(...)`` dict (the
+        reference's temperature / top-p sampler and logit processors, one
+        seed per sequence).  Returns device tensors (sampled [n, new_tokens],
+        n_sampled [n], stop_reason [n], step_logits or None, caches, workspace).
+        Does not synchronise.
         """
         n = int(prompts.shape[0])
         if caches is None:
@@ -315,16 +318,52 @@ class Q6WCudaTransformer:
             with torch.cuda.device(dev):
                 prefill_event.record()  # torch creates the CUDA event on its first record
         ga.prefill_event = prefill_event.cuda_event if prefill_event is not None else None
+        sa = None
+        if sampling is not None:
+            seeds = sampling["seeds"]
+            if seeds.numel() != n:
+                raise ValueError("one seed per sequence")
+            seeds = seeds.to(dev, torch.int64).contiguous()
+            sa = _lib.SampleArgs(float(sampling["temperature"]), float(sampling["top_p"]),
+                                 float(sampling["repetition_penalty"]), int(sampling["no_repeat_ngram_size"]),
+                                 float(sampling["stop_token_bias"]), int(sampling["stop_token_bias_after"]),
+                                 seeds.data_ptr())
+            self._seeds = seeds  # alive until the init kernel has read it
         with torch.cuda.device(dev):
-            _lib.check(self._lib.q6w_generate_greedy(self._handle, ga, ws.data_ptr(), nbytes, _lib.stream_handle()),
-                       "q6w_generate_greedy")
+            if sa is None:
+                _lib.check(self._lib.q6w_generate_greedy(self._handle, ga, ws.data_ptr(), nbytes,
+                                                         _lib.stream_handle()), "q6w_generate_greedy")
+            else:
+                _lib.check(self._lib.q6w_generate(self._handle, ga, sa, ws.data_ptr(), nbytes, _lib.stream_handle()),
+                           "q6w_generate")
         return sampled, n_sampled, stop_reason, step_logits, caches, ws
 
-    def generate_greedy(self, prompts, new_tokens, stop_ids=(), min_new_tokens=0, keep_logits=False):
+    def generate_sampled(self, prompts, new_tokens, seeds, stop_ids=(), min_new_tokens=0, temperature=0.0,
+                         top_p=0.9, repetition_penalty=1.0, stop_token_bias=0.0, stop_token_bias_after=None,
+                         no_repeat_ngram_size=0, keep_logits=False):
+        """Generation with the reference's sampler for a list of prompts, one
+        XorShift64 seed per prompt: each sequence follows
+        torch_benchmark.generate (:233-296) with those arguments.  Host results
+        as ``generate_greedy``."""
+        bias_after = min_new_tokens if stop_token_bias_after is None else stop_token_bias_after
+        if (repetition_penalty <= 0 or not np.isfinite(stop_token_bias) or min_new_tokens < 0
+                or min_new_tokens > new_tokens or bias_after < 0 or no_repeat_ngram_size < 0):
+            raise ValueError("repetition_penalty must be positive, stop_token_bias finite, min_new_tokens within the "
+                             "limit, and bias/ngram settings nonnegative")
+        seeds = [int(s) & ((1 << 64) - 1) for s in seeds]
+        if len(seeds) != len(prompts):
+            raise ValueError("one seed per prompt")
+        signed = [s - (1 << 64) if s >= (1 << 63) else s for s in seeds]  # int64 storage of the u64 seeds
+        sampling = sampling_args(temperature, top_p, repetition_penalty, no_repeat_ngram_size,
+                                 stop_token_bias if stop_ids else 0.0, bias_after,
+                                 torch.tensor(signed, dtype=torch.int64, device=self.device))
+        return self.generate_greedy(prompts, new_tokens, stop_ids, min_new_tokens, keep_logits, sampling=sampling)
+
+    def generate_greedy(self, prompts, new_tokens, stop_ids=(), min_new_tokens=0, keep_logits=False, sampling=None):
         """Greedy generation for a list of prompt id lists; host results.
 
         Contract of prepare_e2e.py:121-143 / torch_benchmark.generate at
-        temperature 0, per sequence.
+        temperature 0, per sequence (``sampling``: see ``generate_sampled``).
         """
         n = len(prompts)
         if n == 0:
@@ -343,7 +382,7 @@ class Q6WCudaTransformer:
         pr = torch.from_numpy(host).to(self.device)
         ln = torch.tensor(lens, dtype=torch.int32, device=self.device)
         sampled, n_sampled, stop_reason, logits, caches, ws = self.generate_greedy_device(
-            pr, ln, L, new_tokens, stop_ids, min_new_tokens, keep_logits=keep_logits)
+            pr, ln, L, new_tokens, stop_ids, min_new_tokens, keep_logits=keep_logits, sampling=sampling)
         self.check_device_status(ws)
         s = sampled.cpu().numpy()
         ns = n_sampled.cpu().numpy()
@@ -365,18 +404,26 @@ def ctypes_void():
     return ctypes.c_void_p()
 
 
+def sampling_args(temperature, top_p, repetition_penalty, no_repeat_ngram_size, stop_token_bias,
+                  stop_token_bias_after, seeds):
+    """The sampler settings of one generation call (q6w_sample_args); ``seeds``
+    a device int64 tensor holding each sequence's 64-bit XorShift64 seed."""
+    return {"temperature": temperature, "top_p": top_p, "repetition_penalty": repetition_penalty,
+            "no_repeat_ngram_size": no_repeat_ngram_size, "stop_token_bias": stop_token_bias,
+            "stop_token_bias_after": stop_token_bias_after, "seeds": seeds}
+
+
 def generate(model, prompt_ids, new_tokens, device=None, stop_token=None, temperature=0.0, top_p=0.9, seed=1,
              repetition_penalty=1.0, min_new_tokens=0, stop_token_bias=0.0, stop_token_bias_after=None,
              no_repeat_ngram_size=0):
     """``torch_benchmark.generate`` (benchmarks/torch_benchmark.py:233-296) on the device.
 
     Same signature, argument checks and return value ``(generated,
-    prefill_seconds, decode_seconds, stopped, stop_reason)``.  Greedy
-    decoding (temperature 0) with stop ids and ``min_new_tokens`` runs as one
-    device-resident loop; prefill and decode times come from CUDA events.
-    The sampling and logit-shaping options (temperature > 0, repetition
-    penalty, stop-token bias, n-gram blocking) are not implemented on the
-    device and raise NotImplementedError.
+    prefill_seconds, decode_seconds, stopped, stop_reason)``.  The whole
+    request runs as one device-resident loop: greedy decoding, or the
+    reference's sampler (XorShift64 seeded with ``seed``, temperature and
+    top-p, repetition penalty, n-gram blocking, stop-id masking and bias) in
+    the step graph.  Prefill and decode times come from CUDA events.
     """
     import math
 
@@ -385,15 +432,18 @@ def generate(model, prompt_ids, new_tokens, device=None, stop_token=None, temper
             or min_new_tokens > new_tokens or bias_after < 0 or no_repeat_ngram_size < 0):
         raise ValueError("repetition_penalty must be positive, stop_token_bias finite, min_new_tokens within the "
                          "limit, and bias/ngram settings nonnegative")
-    if temperature != 0 or repetition_penalty != 1.0 or no_repeat_ngram_size != 0 or (
-            stop_token is not None and stop_token_bias != 0):
-        raise NotImplementedError("only greedy decoding (temperature 0, no logit shaping) runs on the device")
     if new_tokens < 1:
         return [], 0.0, 0.0, False, None
     stops = () if stop_token is None else (tuple(stop_token) if isinstance(stop_token, (set, tuple, list))
                                           else (stop_token,))
     P = len(prompt_ids)
     dev = model.device
+    sampling = None
+    if temperature != 0 or repetition_penalty != 1.0 or no_repeat_ngram_size != 0 or (stops and stop_token_bias != 0):
+        s = int(seed) & ((1 << 64) - 1)
+        sampling = sampling_args(temperature, top_p, repetition_penalty, no_repeat_ngram_size,
+                                 stop_token_bias if stops else 0.0, bias_after,
+                                 torch.tensor([s - (1 << 64) if s >= (1 << 63) else s], dtype=torch.int64, device=dev))
     pr = torch.tensor([list(prompt_ids)], dtype=torch.int32, device=dev)
     ln = torch.tensor([P], dtype=torch.int32, device=dev)
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
@@ -401,7 +451,7 @@ def generate(model, prompt_ids, new_tokens, device=None, stop_token=None, temper
     e0.record()
     e1.record()  # creates the event; the device loop re-records it after the prefill steps
     sampled, n_sampled, stop_reason, _, _, ws = model.generate_greedy_device(
-        pr, ln, P, new_tokens, stops, min_new_tokens, prefill_event=e1)
+        pr, ln, P, new_tokens, stops, min_new_tokens, prefill_event=e1, sampling=sampling)
     e2.record()
     model.check_device_status(ws)
     picks = sampled[0, : int(n_sampled[0])].tolist()

@@ -206,6 +206,39 @@ def linear_argmax(x, packed, scales, rows, columns, want_logits=False):
     return am, lg
 
 
+def sample(logits, history, history_len, rng_state, temperature, top_p=0.9, repetition_penalty=1.0,
+           no_repeat_ngram_size=0, stop_ids=(), min_new_tokens=0, stop_token_bias=0.0, stop_token_bias_after=None):
+    """The reference's per-step sampling (torch_benchmark.py:272-285) on rows
+    of logits, on the GPU: repetition penalty and n-gram blocking over each
+    row's ``history`` (its first ``history_len`` tokens; history_len is also
+    the decode index), stop-id masking / bias, then temperature / top-p
+    sampling from each row's XorShift64 state.
+
+    logits [n, V] float32; history [n, H] int32; history_len [n] int32;
+    rng_state [n] int64 (the generator states, advanced in place).  Returns
+    int32 tokens [n].
+    """
+    n, V = logits.shape
+    lg = logits.contiguous()
+    hist = history.to(torch.int32).contiguous()
+    hl = history_len.to(torch.int32).contiguous()
+    if rng_state.dtype != torch.int64 or not rng_state.is_contiguous():
+        raise ValueError("rng_state must be a contiguous int64 tensor")
+    out = torch.empty(n, dtype=torch.int32, device=logits.device)
+    stop = sorted(set(int(t) for t in stop_ids))
+    arr = (_lib.c_int32 * max(1, len(stop)))(*stop) if stop else None
+    bias_after = min_new_tokens if stop_token_bias_after is None else stop_token_bias_after
+    sa = _lib.SampleArgs(float(temperature), float(top_p), float(repetition_penalty), int(no_repeat_ngram_size),
+                         float(stop_token_bias), int(bias_after), None)
+    lib = _lib.load()
+    with torch.cuda.device(logits.device):
+        _lib.check(lib.q6w_sample(lg.data_ptr(), V, n, V, hist.data_ptr() if hist.numel() else None,
+                                  hist.shape[1] if hist.dim() == 2 else 0, hl.data_ptr(), rng_state.data_ptr(), sa,
+                                  arr, len(stop), int(min_new_tokens), out.data_ptr(), _lib.stream_handle()),
+                   "q6w_sample")
+    return out
+
+
 def rmsnorm(x, weight, eps):
     """Row-wise RMSNorm of x [..., length] (torch_benchmark.py:22-24)."""
     xs = x.reshape(-1, x.shape[-1]).contiguous()
