@@ -193,6 +193,19 @@ typedef struct q6w_model q6w_model;
 Q6W_API int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out);
 Q6W_API void q6w_model_destroy(q6w_model* model);
 
+enum { Q6W_KV_F32 = 0, Q6W_KV_F16 = 1 };
+
+/* Storage type of the KV cache for every later call on this model (default
+ * Q6W_KV_F32).  With Q6W_KV_F16 the k_cache / v_cache arguments point at
+ * IEEE half elements (same [.., max_seq_len, n_kv_heads, head_dim] layout
+ * and element strides, half the bytes): the new K and V rows are rounded to
+ * FP16 (nearest even) when written and widened exactly when read, and
+ * attention computes in FP32 -- the reference's FP16-KV wrapper
+ * (quantization/compare_kv_cache.py:15-72, FP16KVTransformer).  Available
+ * for head dims 16 / 32 (up to 8 kv heads, groups of 1, 2 or 4) and 64 /
+ * 128; the single-request cluster kernel is not used with it. */
+Q6W_API int32_t q6w_model_set_kv_dtype(q6w_model* model, int32_t kv_dtype);
+
 /* Workspace (device scratch, caller-allocated, 256-byte aligned) needed to
  * run up to max_seqs sequences per call. */
 Q6W_API size_t q6w_workspace_bytes(const q6w_model* model, int32_t max_seqs);

@@ -92,24 +92,30 @@ def _rotate_pairs(x, cos, sin):
 
 
 class OracleModel:
-    """B=1 cached transformer over dequantized Q6 weights (CPU, FP32)."""
+    """B=1 cached transformer over dequantized Q6 weights (CPU, FP32).
 
-    def __init__(self, args, state):
+    ``kv_dtype=torch.float16`` restates the reference's FP16-KV wrapper
+    (quantization/compare_kv_cache.py:15-72): the cache holds FP16 (the new
+    rows rounded by ``copy_``) and is read back with ``.float()``.
+    """
+
+    def __init__(self, args, state, kv_dtype=torch.float32):
         self.args = args
         self.w = {k: v.float().contiguous() for k, v in state.items()}
         self.freqs_cos, self.freqs_sin = rope_tables(args)
         self.hidden_dim = args.ffn_dim
+        self.kv_dtype = kv_dtype
 
     @classmethod
-    def from_q6w(cls, binary_path, manifest_path, max_seq_len=None):
+    def from_q6w(cls, binary_path, manifest_path, max_seq_len=None, kv_dtype=torch.float32):
         state, manifest = load_state(binary_path, manifest_path)
-        return cls(OracleArgs.from_model_args(manifest["model_args"], max_seq_len), state)
+        return cls(OracleArgs.from_model_args(manifest["model_args"], max_seq_len), state, kv_dtype)
 
     def new_cache(self, device="cpu"):
         """torch_benchmark.py:87-94 (zero-filled here; unread slots never matter)."""
         a = self.args
         shape = (a.n_layers, a.max_seq_len, a.kv_heads, a.head_dim)
-        return torch.zeros(shape), torch.zeros(shape)
+        return torch.zeros(shape, dtype=self.kv_dtype), torch.zeros(shape, dtype=self.kv_dtype)
 
     def step(self, token_id, position, key_cache, value_cache):
         """One cached decode step; returns logits [vocab] (torch_benchmark.py:96-125)."""
@@ -129,8 +135,8 @@ class OracleModel:
             k = _rotate_pairs(k, cos, sin)
             key_cache[l, position].copy_(k[0, 0])
             value_cache[l, position].copy_(v[0, 0])
-            ks = key_cache[l, : position + 1].permute(1, 0, 2).repeat_interleave(rep, dim=0).unsqueeze(0)
-            vs = value_cache[l, : position + 1].permute(1, 0, 2).repeat_interleave(rep, dim=0).unsqueeze(0)
+            ks = key_cache[l, : position + 1].float().permute(1, 0, 2).repeat_interleave(rep, dim=0).unsqueeze(0)
+            vs = value_cache[l, : position + 1].float().permute(1, 0, 2).repeat_interleave(rep, dim=0).unsqueeze(0)
             att = torch.softmax((torch.matmul(q, ks.transpose(-2, -1)) / denom).float(), dim=-1).type_as(q)
             o = torch.matmul(att, vs).transpose(1, 2).contiguous().view(1, 1, -1)
             x = x + F.linear(o, w[p + "attention.wo.weight"])
@@ -226,10 +232,10 @@ class BatchScorer:
             q = rot(F.linear(u, w[p + "attention.wq.weight"]).view(B, 1, H, hd)).transpose(1, 2)
             k = rot(F.linear(u, w[p + "attention.wk.weight"]).view(B, 1, KV, hd))
             v = F.linear(u, w[p + "attention.wv.weight"]).view(B, KV, hd)
-            kc[rows, l, positions] = k[:, 0]
-            vc[rows, l, positions] = v
-            ks = kc[rows, l, :T].permute(0, 2, 1, 3).repeat_interleave(rep, dim=1)  # [B,H,T,hd]
-            vs = vc[rows, l, :T].permute(0, 2, 1, 3).repeat_interleave(rep, dim=1)
+            kc[rows, l, positions] = k[:, 0].to(kc.dtype)  # an FP16 cache rounds as copy_ does
+            vc[rows, l, positions] = v.to(vc.dtype)
+            ks = kc[rows, l, :T].float().permute(0, 2, 1, 3).repeat_interleave(rep, dim=1)  # [B,H,T,hd]
+            vs = vc[rows, l, :T].float().permute(0, 2, 1, 3).repeat_interleave(rep, dim=1)
             sc = torch.matmul(q, ks.transpose(-2, -1)) / denom  # [B,H,1,T]
             sc = sc.masked_fill(mask, -float("inf"))
             o = torch.matmul(torch.softmax(sc, dim=-1), vs).transpose(1, 2).reshape(B, 1, -1)
@@ -263,7 +269,7 @@ class BatchScorer:
             B = len(idx)
             steps = max(len(f) for f in feeds)
             shape = (B, a.n_layers, a.max_seq_len, a.kv_heads, a.head_dim)
-            kc, vc = torch.zeros(shape), torch.zeros(shape)
+            kc, vc = torch.zeros(shape, dtype=self.m.kv_dtype), torch.zeros(shape, dtype=self.m.kv_dtype)
             with torch.inference_mode():
                 for t in range(steps):
                     live = [j for j in range(B) if t < len(feeds[j])]

@@ -185,7 +185,7 @@ def verify_sampled(scorer, prompts, streams, seeds, new_tokens, stop_token=None,
         feeds.append(list(prompts[i]) + gen[: new_tokens - 1])
     steps = max(len(f) for f in feeds)
     shape = (B, a.n_layers, a.max_seq_len, a.kv_heads, a.head_dim)
-    kc, vc = torch.zeros(shape), torch.zeros(shape)
+    kc, vc = torch.zeros(shape, dtype=scorer.m.kv_dtype), torch.zeros(shape, dtype=scorer.m.kv_dtype)
     with torch.inference_mode():
         for t in range(steps):
             live = [j for j in range(B) if t < len(feeds[j])]

@@ -128,3 +128,25 @@ def test_xorshift_known_values():
         want.append((((s * 0x2545F4914F6CDD1D) & mask) >> 40) / 16777216.0)
     r = XorShift64(1)
     assert [r.random_f32() for _ in range(3)] == want
+
+
+def test_oracle_fp16_kv_matches_reference_wrapper(tiny_files):
+    """OracleModel(kv_dtype=float16) against the reference's FP16KVTransformer
+    (quantization/compare_kv_cache.py:15-72) on the golden request."""
+    import json
+
+    from conftest import GOLDEN
+
+    doc = json.loads((GOLDEN / "fp16_kv.json").read_text())
+    rows = np.load(GOLDEN / "fp16_kv_logits.npz")["rows"]
+    torch.set_num_threads(1)
+    orc = OracleModel.from_q6w(*tiny_files, kv_dtype=torch.float16)
+    assert greedy_request(orc, doc["prompt"], 128)["generated"] == doc["generated"]
+    k, v = orc.new_cache()
+    got = []
+    with torch.inference_mode():
+        for pos, tok in enumerate(doc["prompt"] + doc["generated"][:4]):
+            lg = orc.step(tok, pos, k, v)
+            if pos >= len(doc["prompt"]) - 1:
+                got.append(lg.numpy())
+    assert np.array_equal(np.stack(got), rows)  # the same torch CPU operations: bit for bit

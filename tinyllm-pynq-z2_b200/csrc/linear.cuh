@@ -21,6 +21,8 @@
 // FP32 FMA, so results differ from the reference only by summation order.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace q6w {
@@ -56,6 +58,7 @@ struct EpiArgs {
   const float* rope_cos;
   const float* rope_sin;
   int32_t hd, q_rows, kv_rows;
+  int32_t kv_half;     // the cache holds FP16 (kc / vc point at __half; offsets stay in elements)
   // per-sequence state
   const int32_t* pos;
   const int32_t* flags;
@@ -72,6 +75,73 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// ---- KV cache elements: FP32, or FP16 (round to nearest even, as torch's
+// copy_ of an FP32 row into a float16 cache; quantization/compare_kv_cache.py:57-58)
+
+// Two consecutive elements (offset even) of a cache row.
+__device__ __forceinline__ void store_kv2(float* base, int64_t off, int half, float a, float b) {
+  if (half)
+    *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(base) + off) = __floats2half2_rn(a, b);
+  else
+    *reinterpret_cast<float2*>(base + off) = make_float2(a, b);
+}
+
+// Eight consecutive elements (offset a multiple of 8) of a cache row.
+__device__ __forceinline__ void store_kv8(float* base, int64_t off, int half, float4 p0, float4 p1) {
+  if (half) {
+    const __half2 h0 = __floats2half2_rn(p0.x, p0.y), h1 = __floats2half2_rn(p0.z, p0.w);
+    const __half2 h2 = __floats2half2_rn(p1.x, p1.y), h3 = __floats2half2_rn(p1.z, p1.w);
+    uint4 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&h0);
+    u.y = *reinterpret_cast<const uint32_t*>(&h1);
+    u.z = *reinterpret_cast<const uint32_t*>(&h2);
+    u.w = *reinterpret_cast<const uint32_t*>(&h3);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(base) + off) = u;
+  } else {
+    reinterpret_cast<float4*>(base + off)[0] = p0;
+    reinterpret_cast<float4*>(base + off)[1] = p1;
+  }
+}
+
+// Four consecutive cache elements as FP32 (FP16 converts exactly).
+template <typename KT>
+__device__ __forceinline__ float4 load_kv4(const KT* p);
+template <>
+__device__ __forceinline__ float4 load_kv4<float>(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+template <>
+__device__ __forceinline__ float4 load_kv4<__half>(const __half* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// Sixteen consecutive cache elements as four float4.
+template <typename KT>
+__device__ __forceinline__ void load_kv16(const KT* p, float4 (&o)[4]);
+template <>
+__device__ __forceinline__ void load_kv16<float>(const float* p, float4 (&o)[4]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = q[i];
+}
+template <>
+__device__ __forceinline__ void load_kv16<__half>(const __half* p, float4 (&o)[4]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint4 u = q[i];
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+    o[2 * i] = make_float4(a.x, a.y, b.x, b.y);
+    o[2 * i + 1] = make_float4(c.x, c.y, d.x, d.y);
+  }
 }
 
 __device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) {
@@ -141,18 +211,18 @@ __device__ __forceinline__ unsigned long long epilogue(const EpiArgs& ep, int m,
       a = ra;
       b = rb;
     }
-    float* dst;
     const int64_t crow = ep.seq ? ep.seq[m] : m;
     if (v < ep.q_rows) {
-      dst = ep.qbuf + (int64_t)m * ep.ldq + v;
-    } else if (v < ep.q_rows + ep.kv_rows) {
-      dst = ep.kc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (v - ep.q_rows);
+      float* dst = ep.qbuf + (int64_t)m * ep.ldq + v;
+      dst[0] = a;
+      dst[1] = b;
     } else {
-      dst = ep.vc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
-            (v - ep.q_rows - ep.kv_rows);
+      const bool kr = v < ep.q_rows + ep.kv_rows;
+      const int64_t off = crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
+                          (kr ? v - ep.q_rows : v - ep.q_rows - ep.kv_rows);
+      float* base = kr ? ep.kc : ep.vc;
+      store_kv2(base, off, ep.kv_half, a, b);
     }
-    dst[0] = a;
-    dst[1] = b;
   } else if (EPI == EPI_VOCAB) {
     const int r = 2 * p;
     if (ep.y) {

@@ -78,6 +78,7 @@ struct q6w_model {
   bool use_tcg = false; // shapes qualify for the general tensor-core linears (any width)
   int sm_count = 148;
   bool use_b1 = false;  // shapes qualify for the single-request cluster kernel
+  bool kv_half = false; // the KV cache holds FP16 (q6w_model_set_kv_dtype)
   size_t b1_smem = 0;
 };
 
@@ -302,9 +303,9 @@ __global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ qb,
 // (4-dim column, position stride) to accumulate probability * V, merged in a
 // fixed order.  Softmax as torch: exp(s - max), divide by the sum, then the
 // weighted sum of V rows (torch_benchmark.py:114-119).
-template <int HD>
+template <int HD, typename KT = float>
 __global__ void __launch_bounds__(256) attn_head_kernel(
-    const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+    const float* __restrict__ qb, int ldq, const KT* __restrict__ kc, const KT* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
     const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int H, int KV, int S, float denom,
     const int32_t* __restrict__ seq) {
@@ -327,17 +328,17 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
   const int kvr = KV * HD;
   const int g = h / (H / KV);
   const int64_t crow = seq ? seq[b] : b;
-  const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + g * HD);
-  const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + g * HD);
+  const KT* kb = kc + crow * cstride + layer_off + g * HD;
+  const KT* vb = vc + crow * cstride + layer_off + g * HD;
   if (tid < HD) sq[tid] = qb[(int64_t)b * ldq + h * HD + tid];
   __syncthreads();
   float mx = -INFINITY;
   for (int t = tid; t < T; t += 256) {
-    const float4* kr = kb + (int64_t)t * (kvr / 4);
+    const KT* kr = kb + (int64_t)t * kvr;
     float d = 0.0f;
 #pragma unroll
     for (int j = 0; j < CQ; ++j) {
-      const float4 k4 = __ldg(kr + j);
+      const float4 k4 = load_kv4(kr + 4 * j);
       d = fmaf(sq[4 * j], k4.x, d);
       d = fmaf(sq[4 * j + 1], k4.y, d);
       d = fmaf(sq[4 * j + 2], k4.z, d);
@@ -370,7 +371,7 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = grp; t < T; t += G) {
     const float wt = __fdiv_rn(sp[t], sum);
-    const float4 v4 = __ldg(vb + (int64_t)t * (kvr / 4) + cq);
+    const float4 v4 = load_kv4(vb + (int64_t)t * kvr + 4 * cq);
     acc.x = fmaf(wt, v4.x, acc.x);
     acc.y = fmaf(wt, v4.y, acc.y);
     acc.z = fmaf(wt, v4.z, acc.z);
@@ -395,9 +396,9 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
 // outputs are bit-identical to it.
 // STAGE_V: the group's V rows [0, T) are copied into shared memory (cp.async)
 // at the start, so their latency hides behind the score phase.
-template <int HD, int REP, bool STAGE_V>
+template <int HD, int REP, bool STAGE_V, typename KT = float>
 __global__ void __launch_bounds__(256) attn_group_kernel(
-    const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+    const float* __restrict__ qb, int ldq, const KT* __restrict__ kc, const KT* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
     const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int KV, int S, float denom,
     const int32_t* __restrict__ seq) {
@@ -420,13 +421,14 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
   }
   const int kvr = KV * HD;
   const int64_t crow = seq ? seq[b] : b;
-  const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + g * HD);
-  const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + g * HD);
+  const KT* kb = kc + crow * cstride + layer_off + g * HD;
+  const KT* vb = vc + crow * cstride + layer_off + g * HD;
+  static_assert(!STAGE_V || sizeof(KT) == 4, "V staging copies FP32 rows");
   if (STAGE_V) {
     for (int i = tid; i < T * CQ; i += 256) {
       const int t = i / CQ, c = i % CQ;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sv + i)),
-                   "l"(vb + (int64_t)t * (kvr / 4) + c)
+                   "l"(vb + (int64_t)t * kvr + 4 * c)
                    : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -437,13 +439,13 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
 #pragma unroll
   for (int r = 0; r < REP; ++r) mx[r] = -INFINITY;
   for (int t = tid; t < T; t += 256) {
-    const float4* kr = kb + (int64_t)t * (kvr / 4);
+    const KT* kr = kb + (int64_t)t * kvr;
     float d[REP];
 #pragma unroll
     for (int r = 0; r < REP; ++r) d[r] = 0.0f;
 #pragma unroll
     for (int j = 0; j < CQ; ++j) {
-      const float4 k4 = __ldg(kr + j);
+      const float4 k4 = load_kv4(kr + 4 * j);
 #pragma unroll
       for (int r = 0; r < REP; ++r) {
         const float4 q4 = reinterpret_cast<const float4*>(sq + r * HD)[j];
@@ -504,7 +506,7 @@ __global__ void __launch_bounds__(256) attn_group_kernel(
 #pragma unroll
   for (int r = 0; r < REP; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = grp; t < T; t += G) {
-    const float4 v4 = STAGE_V ? sv[t * CQ + cq] : __ldg(vb + (int64_t)t * (kvr / 4) + cq);
+    const float4 v4 = STAGE_V ? sv[t * CQ + cq] : load_kv4(vb + (int64_t)t * kvr + 4 * cq);
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       const float wt = __fdiv_rn(sp[r * S + t], sum[r]);
@@ -557,23 +559,31 @@ static void attn_group_setup() {
 static size_t attn_head_smem(int hd, int S) { return (size_t)(hd + 16) * 4 + 256 * 16 + (size_t)S * 4; }
 
 static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, const float* qb, int ldq,
-                             const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
+                             const void* kc, const void* vc, int64_t cstride, int64_t layer_off,
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo, int S,
-                             float denom, const int32_t* seq = nullptr) {
+                             float denom, const int32_t* seq = nullptr, bool kv_half = false) {
+  const float* kf = static_cast<const float*>(kc);
+  const float* vf = static_cast<const float*>(vc);
+  const __half* kh = static_cast<const __half*>(kc);
+  const __half* vh = static_cast<const __half*>(vc);
   // many (sequence, kv head) pairs: one CTA per pair serves the group's query heads
   const int rep = KV > 0 ? H / KV : 0;
-  const bool stage = g_attn_stage_ok && attn_group_smem(hd, rep, S, true) <= kAttnStageMax;
+  const bool stage = !kv_half && g_attn_stage_ok && attn_group_smem(hd, rep, S, true) <= kAttnStageMax;
   if (n * KV >= 128 && KV * rep == H && KV <= 65535 && (rep == 2 || rep == 4 || rep == 8) &&
       (hd == 64 || hd == 128) && (stage || attn_group_smem(hd, rep, S, false) <= 48 * 1024)) {
     const dim3 ggrid(n, KV);
     const size_t gsm = attn_group_smem(hd, rep, S, stage);
-#define Q6W_GROUP(HDV, REPV)                                                                                    \
-  if (hd == HDV && rep == REPV) {                                                                               \
-    if (stage)                                                                                                  \
-      attn_group_kernel<HDV, REPV, true><<<ggrid, 256, gsm, st>>>(qb, ldq, kc, vc, cstride, layer_off, len,     \
-                                                                  len_add, flags, out, ldo, KV, S, denom, seq); \
-    else                                                                                                        \
-      attn_group_kernel<HDV, REPV, false><<<ggrid, 256, gsm, st>>>(qb, ldq, kc, vc, cstride, layer_off, len,    \
+#define Q6W_GROUP(HDV, REPV)                                                                                     \
+  if (hd == HDV && rep == REPV) {                                                                                \
+    if (kv_half)                                                                                                 \
+      attn_group_kernel<HDV, REPV, false, __half><<<ggrid, 256, gsm, st>>>(qb, ldq, kh, vh, cstride, layer_off, \
+                                                                           len, len_add, flags, out, ldo, KV, S, \
+                                                                           denom, seq);                          \
+    else if (stage)                                                                                              \
+      attn_group_kernel<HDV, REPV, true><<<ggrid, 256, gsm, st>>>(qb, ldq, kf, vf, cstride, layer_off, len,      \
+                                                                  len_add, flags, out, ldo, KV, S, denom, seq);  \
+    else                                                                                                         \
+      attn_group_kernel<HDV, REPV, false><<<ggrid, 256, gsm, st>>>(qb, ldq, kf, vf, cstride, layer_off, len,     \
                                                                    len_add, flags, out, ldo, KV, S, denom, seq); \
   }
     Q6W_GROUP(64, 2) Q6W_GROUP(64, 4) Q6W_GROUP(64, 8) Q6W_GROUP(128, 2) Q6W_GROUP(128, 4) Q6W_GROUP(128, 8)
@@ -583,13 +593,28 @@ static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, cons
   const size_t smem = attn_head_smem(hd, S);
   if (smem > 48 * 1024 || H > 65535 || (hd != 64 && hd != 128)) return false;
   const dim3 grid(n, H);
-  if (hd == 64)
-    attn_head_kernel<64><<<grid, 256, smem, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add, flags, out,
+  if (hd == 64 && kv_half)
+    attn_head_kernel<64, __half><<<grid, 256, smem, st>>>(qb, ldq, kh, vh, cstride, layer_off, len, len_add, flags,
+                                                          out, ldo, H, KV, S, denom, seq);
+  else if (hd == 64)
+    attn_head_kernel<64><<<grid, 256, smem, st>>>(qb, ldq, kf, vf, cstride, layer_off, len, len_add, flags, out,
                                                   ldo, H, KV, S, denom, seq);
+  else if (kv_half)
+    attn_head_kernel<128, __half><<<grid, 256, smem, st>>>(qb, ldq, kh, vh, cstride, layer_off, len, len_add,
+                                                           flags, out, ldo, H, KV, S, denom, seq);
   else
-    attn_head_kernel<128><<<grid, 256, smem, st>>>(qb, ldq, kc, vc, cstride, layer_off, len, len_add, flags, out,
+    attn_head_kernel<128><<<grid, 256, smem, st>>>(qb, ldq, kf, vf, cstride, layer_off, len, len_add, flags, out,
                                                    ldo, H, KV, S, denom, seq);
   return true;
+}
+
+// Whether FP16 KV storage is served for this head layout: the warp kernel
+// (head dims 16 / 32 with an instantiated kv-head count and group size) or
+// the group / per-head kernels (head dims 64 / 128).
+static bool attn_rows_instantiated(int hd, int KV, int rep) {
+  const bool k16 = hd == 16 && (KV == 1 || KV == 2 || KV == 4 || KV == 8) && (rep == 1 || rep == 2 || rep == 4);
+  const bool k32 = hd == 32 && (KV == 1 || KV == 2 || KV == 4) && (rep == 1 || rep == 2 || rep == 4);
+  return k16 || k32;
 }
 
 // Decode attention, one warp per sequence: the warp streams the sequence's
@@ -597,9 +622,9 @@ static bool launch_attn_head(int hd, int n, int H, int KV, cudaStream_t st, cons
 // 16 dims per lane), prefetching the next pass's rows while it computes the
 // current one, with an online softmax per lane for the REP query heads of
 // its kv head; lanes holding the same (kv head, dims) merge by shuffles.
-template <int HD, int KV, int REP, bool SPLIT>
+template <int HD, int KV, int REP, bool SPLIT, typename KT = float>
 __global__ void __launch_bounds__(128) attn_warp_kernel(
-    const float* __restrict__ qb, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+    const float* __restrict__ qb, int ldq, const KT* __restrict__ kc, const KT* __restrict__ vc,
     int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
     const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom, int n,
     uint8_t* __restrict__ out_img, const int32_t* __restrict__ seq) {
@@ -642,17 +667,16 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
     for (int i = 0; i < 16; ++i) acc[j][i] = 0.0f;
   }
   const int64_t crow = seq ? seq[b] : b;
-  const float4* kb = reinterpret_cast<const float4*>(kc + crow * cstride + layer_off + r * 16);
-  const float4* vb = reinterpret_cast<const float4*>(vc + crow * cstride + layer_off + r * 16);
+  const KT* kb = kc + crow * cstride + layer_off + r * 16;
+  const KT* vb = vc + crow * cstride + layer_off + r * 16;
   const int t_lane = lane / R;
   float4 kn[4], vn[4];
-  {
-    const bool act = t_lane < T;
+  if (t_lane < T) {
+    load_kv16(kb + (int64_t)t_lane * ROW, kn);
+    load_kv16(vb + (int64_t)t_lane * ROW, vn);
+  } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      kn[i] = act ? kb[(int64_t)t_lane * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      vn[i] = act ? vb[(int64_t)t_lane * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int i = 0; i < 4; ++i) kn[i] = vn[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int t0 = 0; t0 < T; t0 += PPW) {
     const int t = t0 + t_lane;
@@ -664,11 +688,12 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
       vv[4 * i] = vn[i].x; vv[4 * i + 1] = vn[i].y; vv[4 * i + 2] = vn[i].z; vv[4 * i + 3] = vn[i].w;
     }
     const int tn = t + PPW;
-    const bool actn = tn < T;
+    if (tn < T) {
+      load_kv16(kb + (int64_t)tn * ROW, kn);
+      load_kv16(vb + (int64_t)tn * ROW, vn);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      kn[i] = actn ? kb[(int64_t)tn * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      vn[i] = actn ? vb[(int64_t)tn * (ROW / 4) + i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < 4; ++i) kn[i] = vn[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int j = 0; j < REP; ++j) {
@@ -735,21 +760,36 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
 // Launch the streaming kernel when the shape has an instantiation; returns
 // false to fall back to the per-head kernel.
 static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st, const float* qb, int ldq,
-                             const float* kc, const float* vc, int64_t cstride, int64_t layer_off,
+                             const void* kc, const void* vc, int64_t cstride, int64_t layer_off,
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo,
-                             int S, float denom, uint8_t* out_img = nullptr, const int32_t* seq = nullptr) {
-#define Q6W_ROWS(HDV, KVV, REPV)                                                                          \
-  if (hd == HDV && KV == KVV && rep == REPV) {                                                            \
-    const int nb = ((int)grid.x + 3) / 4;                                                                 \
-    if (out_img)                                                                                          \
-      attn_warp_kernel<HDV, KVV, REPV, true><<<nb, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,      \
-                                                                 len, len_add, flags, out, ldo, S,        \
-                                                                 denom, (int)grid.x, out_img, seq);       \
-    else                                                                                                  \
-      attn_warp_kernel<HDV, KVV, REPV, false><<<nb, 128, 0, st>>>(qb, ldq, kc, vc, cstride, layer_off,     \
-                                                                  len, len_add, flags, out, ldo, S,       \
-                                                                  denom, (int)grid.x, nullptr, seq);      \
-    return true;                                                                                          \
+                             int S, float denom, uint8_t* out_img = nullptr, const int32_t* seq = nullptr,
+                             bool kv_half = false) {
+  const float* kf = static_cast<const float*>(kc);
+  const float* vf = static_cast<const float*>(vc);
+  const __half* kh = static_cast<const __half*>(kc);
+  const __half* vh = static_cast<const __half*>(vc);
+#define Q6W_ROWS(HDV, KVV, REPV)                                                                           \
+  if (hd == HDV && KV == KVV && rep == REPV) {                                                             \
+    const int nb = ((int)grid.x + 3) / 4;                                                                  \
+    if (kv_half && out_img)                                                                                \
+      attn_warp_kernel<HDV, KVV, REPV, true, __half><<<nb, 128, 0, st>>>(qb, ldq, kh, vh, cstride,         \
+                                                                         layer_off, len, len_add, flags,   \
+                                                                         out, ldo, S, denom, (int)grid.x,  \
+                                                                         out_img, seq);                    \
+    else if (kv_half)                                                                                      \
+      attn_warp_kernel<HDV, KVV, REPV, false, __half><<<nb, 128, 0, st>>>(qb, ldq, kh, vh, cstride,        \
+                                                                          layer_off, len, len_add, flags,  \
+                                                                          out, ldo, S, denom, (int)grid.x, \
+                                                                          nullptr, seq);                   \
+    else if (out_img)                                                                                      \
+      attn_warp_kernel<HDV, KVV, REPV, true><<<nb, 128, 0, st>>>(qb, ldq, kf, vf, cstride, layer_off,      \
+                                                                 len, len_add, flags, out, ldo, S,         \
+                                                                 denom, (int)grid.x, out_img, seq);        \
+    else                                                                                                   \
+      attn_warp_kernel<HDV, KVV, REPV, false><<<nb, 128, 0, st>>>(qb, ldq, kf, vf, cstride, layer_off,     \
+                                                                  len, len_add, flags, out, ldo, S,        \
+                                                                  denom, (int)grid.x, nullptr, seq);       \
+    return true;                                                                                           \
   }
   Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)
   Q6W_ROWS(16, 1, 2) Q6W_ROWS(16, 2, 2) Q6W_ROWS(16, 4, 2) Q6W_ROWS(16, 8, 2)
@@ -840,6 +880,7 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
   ep.pos = w.pos;
   ep.flags = w.flags;
   ep.seq = w.seq;
+  ep.kv_half = M->kv_half;
   const int warps = d.n_heads < 8 ? d.n_heads : 8;
   const dim3 agrid(n, (d.n_heads + warps - 1) / warps);
   const size_t asmem = (size_t)warps * S * sizeof(float);
@@ -866,11 +907,13 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
       if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "qkv linear: %s", cudaGetErrorString(e));
     }
     if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
-                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq)) {
+                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq, M->kv_half)) {
       Q6W_LAUNCH_CHECK("attn_rows_kernel");
     } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
-                                w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq)) {
+                                w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq, M->kv_half)) {
       Q6W_LAUNCH_CHECK("attn_head_kernel");
+    } else if (M->kv_half) {
+      return fail(Q6W_ERR_ARG, "no FP16-KV attention kernel for this head layout");
     } else {
     switch (M->hd) {
 #define Q6W_ATTN(HDV)                                                                          \
@@ -1049,6 +1092,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
   base.ep.pos = w.pos;
   base.ep.flags = w.flags;
   base.ep.seq = w.seq;
+  base.ep.kv_half = M->kv_half;
   int32_t rc;
   for (int l = 0; l < d.n_layers; ++l) {
     const q6w_layer_weights& L = M->layers[l];
@@ -1071,7 +1115,8 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       if ((rc = tc_launch(tc::TEPI_QKV, a, M->sm_count, st))) return rc;
     }
     if (!launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, dim3(n), st, w.qb, dim, kc, vc,
-                          cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img, w.seq))
+                          cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img, w.seq,
+                          M->kv_half))
       return fail(Q6W_ERR_ARG, "no attention kernel for this head layout");
     Q6W_LAUNCH_CHECK("attn_rows_kernel");
     {
@@ -1394,6 +1439,7 @@ static int32_t enqueue_step_tcg(const q6w_model* M, int n, const Work& w, float*
   base.ep.pos = w.pos;
   base.ep.flags = w.flags;
   base.ep.seq = w.seq;
+  base.ep.kv_half = M->kv_half;
   int32_t rc;
   const int warps = d.n_heads < 8 ? d.n_heads : 8;
   const dim3 agrid(n, (d.n_heads + warps - 1) / warps);
@@ -1414,11 +1460,13 @@ static int32_t enqueue_step_tcg(const q6w_model* M, int n, const Work& w, float*
       if ((rc = tcg_launch(tcg::GEPI_QKV, a, M->sm_count, st))) return rc;
     }
     if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
-                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq)) {
+                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq, M->kv_half)) {
       Q6W_LAUNCH_CHECK("attn_rows_kernel");
     } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
-                                w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq)) {
+                                w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq, M->kv_half)) {
       Q6W_LAUNCH_CHECK("attn_head_kernel");
+    } else if (M->kv_half) {
+      return fail(Q6W_ERR_ARG, "no FP16-KV attention kernel for this head layout");
     } else {
       return fail(Q6W_ERR_ARG, "no attention kernel for head_dim %d on the tensor-core step", M->hd);
     }
@@ -1644,6 +1692,27 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
     }
   }
   *out = M;
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_model_set_kv_dtype(q6w_model* M, int32_t kv_dtype) {
+  clear_error();
+  if (!M) return fail(Q6W_ERR_ARG, "null model");
+  if (kv_dtype != Q6W_KV_F32 && kv_dtype != Q6W_KV_F16)
+    return fail(Q6W_ERR_ARG, "kv_dtype must be Q6W_KV_F32 or Q6W_KV_F16");
+  if (kv_dtype == Q6W_KV_F16) {
+    const int KV = M->d.n_kv_heads, rep = M->d.n_heads / KV, hd = M->hd;
+    const bool ok = attn_rows_instantiated(hd, KV, rep) ||
+                    ((hd == 64 || hd == 128) && attn_head_smem(hd, M->d.max_seq_len) <= 48 * 1024);
+    if (!ok) return fail(Q6W_ERR_ARG, "FP16 KV storage is not available for head_dim %d with %d kv heads", hd, KV);
+  }
+  const bool half = kv_dtype == Q6W_KV_F16;
+  if (half != M->kv_half && M->exec) {  // the captured step graph bakes in the cache type
+    cudaGraphExecDestroy(M->exec);
+    M->exec = nullptr;
+    M->have_key = false;
+  }
+  M->kv_half = half;
   return Q6W_OK;
 }
 
@@ -1974,7 +2043,7 @@ extern "C" int32_t q6w_generate(q6w_model* M, const q6w_greedy_args* a, const q6
   cudaGetDevice(&dev);
   if (dev != M->device) return fail(Q6W_ERR_ARG, "model was created on device %d, current is %d", M->device, dev);
 
-  if (n == 1 && M->use_b1 && !sampler) {  // one greedy request: the cluster kernel runs the whole loop
+  if (n == 1 && M->use_b1 && !sampler && !M->kv_half) {  // one greedy request: the cluster kernel runs the loop
     cudaStream_t s = (cudaStream_t)stream;
     b1::Args ba;
     b1_fill(M, ba);

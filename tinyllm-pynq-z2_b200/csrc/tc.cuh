@@ -541,16 +541,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
           const int64_t mr = (int64_t)mt * kM + r;
           const float4 p0 = st4[r * 32 + ((cb >> 2) ^ (r & 7))], p1 = st4[r * 32 + (((cb >> 2) + 1) ^ (r & 7))];
           const int v0 = nt * a.N + 128 * b + cb;
-          float* dst;
-          if (v0 < ep.q_rows)
-            dst = ep.qbuf + mr * ep.ldq + v0;
-          else if (v0 < ep.q_rows + ep.kv_rows)
-            dst = ep.kc + s_crow[r] * ep.cache_stride + ep.layer_off + (int64_t)s_pos[r] * ep.kv_rows + (v0 - ep.q_rows);
-          else
-            dst = ep.vc + s_crow[r] * ep.cache_stride + ep.layer_off + (int64_t)s_pos[r] * ep.kv_rows +
-                  (v0 - ep.q_rows - ep.kv_rows);
-          reinterpret_cast<float4*>(dst)[0] = p0;
-          reinterpret_cast<float4*>(dst)[1] = p1;
+          if (v0 < ep.q_rows) {
+            float* dst = ep.qbuf + mr * ep.ldq + v0;
+            reinterpret_cast<float4*>(dst)[0] = p0;
+            reinterpret_cast<float4*>(dst)[1] = p1;
+          } else {
+            const bool kr = v0 < ep.q_rows + ep.kv_rows;
+            const int64_t off = s_crow[r] * ep.cache_stride + ep.layer_off + (int64_t)s_pos[r] * ep.kv_rows +
+                                (kr ? v0 - ep.q_rows : v0 - ep.q_rows - ep.kv_rows);
+            store_kv8(kr ? ep.kc : ep.vc, off, ep.kv_half, p0, p1);
+          }
         }
         __syncthreads();  // the next block reuses sB
       }

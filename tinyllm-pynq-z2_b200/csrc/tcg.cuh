@@ -426,15 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1) tcg_kernel(GArgs a, const __grid_
             ra = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
             rb = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
           }
-          float* dst;
-          if (vrow < ep.q_rows)
-            dst = ep.qbuf + (int64_t)m * ep.ldq + vrow;
-          else if (vrow < ep.q_rows + ep.kv_rows)
-            dst = ep.kc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows + (vrow - ep.q_rows);
-          else
-            dst = ep.vc + crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
-                  (vrow - ep.q_rows - ep.kv_rows);
-          *reinterpret_cast<float2*>(dst) = make_float2(ra, rb);
+          if (vrow < ep.q_rows) {
+            *reinterpret_cast<float2*>(ep.qbuf + (int64_t)m * ep.ldq + vrow) = make_float2(ra, rb);
+          } else {
+            const bool kr = vrow < ep.q_rows + ep.kv_rows;
+            const int64_t off = crow * ep.cache_stride + ep.layer_off + (int64_t)pos * ep.kv_rows +
+                                (kr ? vrow - ep.q_rows : vrow - ep.q_rows - ep.kv_rows);
+            store_kv2(kr ? ep.kc : ep.vc, off, ep.kv_half, ra, rb);
+          }
         }
       } else {  // GEPI_VOCAB: logits, dumped step logits, stop masking, first-maximum key
         if (m < a.n) {  // warp-uniform: a warp holds one activation

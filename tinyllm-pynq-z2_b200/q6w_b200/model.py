@@ -59,7 +59,12 @@ class GreedyResult(SimpleNamespace):
 
 
 class Q6WCudaTransformer:
-    def __init__(self, image, device="cuda", max_seq_len=None):
+    """``kv_dtype``: torch.float32 (the reference's ``CachedTransformer``) or
+    torch.float16 (its FP16-KV wrapper, quantization/compare_kv_cache.py:15-72:
+    K/V rows stored as FP16, attention in FP32); the caches ``new_cache`` and
+    ``new_batch_cache`` return have that dtype."""
+
+    def __init__(self, image, device="cuda", max_seq_len=None, kv_dtype=torch.float32):
         device = torch.device(device)
         if device.type != "cuda":
             raise ValueError("Q6WCudaTransformer runs on a CUDA device")
@@ -83,12 +88,17 @@ class Q6WCudaTransformer:
             _lib.check(self._lib.q6w_model_create(self._desc, handle), "q6w_model_create")
             self._handle = handle
             self._ws = {}
+        if kv_dtype not in (torch.float32, torch.float16):
+            raise ValueError("kv_dtype must be torch.float32 or torch.float16")
+        _lib.check(self._lib.q6w_model_set_kv_dtype(self._handle, 1 if kv_dtype == torch.float16 else 0),
+                   "q6w_model_set_kv_dtype")
+        self.kv_dtype = kv_dtype
 
     # -- construction ----------------------------------------------------------
     @classmethod
-    def from_q6w(cls, binary_path, manifest_path, device="cuda", max_seq_len=None):
+    def from_q6w(cls, binary_path, manifest_path, device="cuda", max_seq_len=None, kv_dtype=torch.float32):
         """Load a Q6W binary + manifest (SHA and header checked) onto ``device``."""
-        return cls(Q6WImage(binary_path, manifest_path), device, max_seq_len)
+        return cls(Q6WImage(binary_path, manifest_path), device, max_seq_len, kv_dtype)
 
     def _qmat(self, name):
         packed, scales, rows, cols = self.dimg.qmat(name)
@@ -162,14 +172,15 @@ class Q6WCudaTransformer:
         dev = self.device if device is None else torch.device(device)
         if dev.type != "cuda":
             raise ValueError("the KV cache must live on the model's CUDA device")
-        return torch.empty(shape, device=self.device), torch.empty(shape, device=self.device)
+        return (torch.empty(shape, device=self.device, dtype=self.kv_dtype),
+                torch.empty(shape, device=self.device, dtype=self.kv_dtype))
 
     def _check_cache(self, k, v, n=None):
         a = self.args
         shape = (a.n_layers, a.max_seq_len, self.n_kv_heads, self.head_dim)
         for c in (k, v):
-            if c.dtype != torch.float32 or c.device != self.device or not c.is_contiguous():
-                raise ValueError("KV cache must be contiguous float32 on the model's device")
+            if c.dtype != self.kv_dtype or c.device != self.device or not c.is_contiguous():
+                raise ValueError(f"KV cache must be contiguous {self.kv_dtype} on the model's device")
             if tuple(c.shape[-4:]) != shape or (n is not None and (c.dim() != 5 or c.shape[0] < n)):
                 raise ValueError(f"KV cache shape {tuple(c.shape)} does not match {shape}")
 
@@ -195,7 +206,8 @@ class Q6WCudaTransformer:
         slice is a ``new_cache`` cache."""
         a = self.args
         shape = (n_seqs, a.n_layers, a.max_seq_len, self.n_kv_heads, self.head_dim)
-        return torch.empty(shape, device=self.device), torch.empty(shape, device=self.device)
+        return (torch.empty(shape, device=self.device, dtype=self.kv_dtype),
+                torch.empty(shape, device=self.device, dtype=self.kv_dtype))
 
     def forward_batch(self, tokens, positions, key_cache, value_cache, logits=True, argmax=False):
         """One cached step of n independent sequences (device int32 tokens/positions).
