@@ -254,6 +254,23 @@ Q6W_API int32_t q6w_prefill(const q6w_model* model, int32_t n_prompts, const int
                     float* last_logits, int32_t* last_argmax, void* workspace, size_t workspace_bytes,
                     q6w_stream_t stream);
 
+/* The non-cached forward with targets -- Transformer.forward(tokens, targets)
+ * of training/model.py:249-269 -- on ragged prompts (arguments and KV-cache
+ * filling as q6w_prefill, same workspace): logits [total_tokens, vocab] of
+ * every position (row off_i + j for position j of prompt i, off_i the sum of
+ * the earlier prompts' lengths; 16-byte aligned), and when targets
+ * [n_prompts, prompt_stride] (device int32) is given, *loss (device, one
+ * float) = the mean cross entropy over the positions whose target is not -1
+ * (F.cross_entropy(..., ignore_index=-1); NaN if every target is -1).  A
+ * target outside [0, vocab) other than -1 is flagged on the device
+ * (q6w_workspace_status) and that position is not counted.  targets and loss
+ * are both NULL or both set. */
+Q6W_API int32_t q6w_forward_all(const q6w_model* model, int32_t n_prompts, const int32_t* prompts,
+                                const int32_t* prompt_lens, int32_t prompt_stride, int32_t max_prompt_len,
+                                int64_t total_tokens, float* k_cache, float* v_cache, int64_t cache_seq_stride,
+                                float* logits, const int32_t* targets, float* loss, void* workspace,
+                                size_t workspace_bytes, q6w_stream_t stream);
+
 /* Greedy generation of n_seqs independent requests, entirely on the device:
  * token-by-token prefill of each (ragged) prompt, then greedy decode with
  * the reference's stop contract -- stop ids masked to -inf while fewer than

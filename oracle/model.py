@@ -197,6 +197,25 @@ def greedy_request(model, prompt_ids, new_tokens, stop_ids=(), min_new_tokens=0,
     return out
 
 
+def forward_all(model, token_rows, target_rows=None):
+    """Logits of every position of each token row, and with targets the mean
+    cross entropy over positions whose target is not -1: the non-cached
+    ``Transformer.forward(tokens, targets)`` of training/model.py:249-269
+    (F.cross_entropy(..., ignore_index=-1)), computed here with the cached
+    step over each row (the same arithmetic up to summation order).
+    Returns (list of [len, vocab] logits, loss or None)."""
+    out = []
+    with torch.inference_mode():
+        for row in token_rows:
+            k, v = model.new_cache()
+            out.append(torch.stack([model.step(int(t), p, k, v) for p, t in enumerate(row)]))
+        loss = None
+        if target_rows is not None:
+            tg = torch.cat([torch.as_tensor(t, dtype=torch.long) for t in target_rows])
+            loss = float(F.cross_entropy(torch.cat(out), tg, ignore_index=-1))
+    return out, loss
+
+
 class BatchScorer:
     """Many-sequence FP32 CPU forward used to verify device token streams.
 

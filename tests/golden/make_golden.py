@@ -247,6 +247,37 @@ def fp16_kv_request(tmp):
     return {"prompt": prompt, "generated": gen}, torch.stack(rows).numpy()
 
 
+def forward_all_request(tmp):
+    """The reference's non-cached forward with targets (training/model.py
+    Transformer.forward, :249-269) on the tiny synthetic model: a [2, 40]
+    token batch whose targets ignore (-1) a few positions; the loss and the
+    logits of every 5th position."""
+    sys.path.insert(0, str(REF / "training"))
+    import model as ref_train
+
+    b, m = tmp / "tinyf.bin", tmp / "tinyf.json"
+    fmt.write_synthetic(fmt.TINY_ARGS, TINY_SEED, b, m)
+    manifest = json.loads(m.read_text())
+    margs = {**DEFAULTS, **manifest["model_args"]}
+    args = ref_train.ModelArgs(**{k: margs[k] for k in ("dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size",
+                                                         "hidden_dim", "multiple_of", "norm_eps", "max_seq_len",
+                                                         "dropout")})
+    model = ref_train.Transformer(args).eval()
+    template = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    state, _ = ref_fmt.load_dequantized_state(b, m, template)
+    model.load_state_dict(state, strict=True)
+    g = torch.Generator().manual_seed(41)
+    tokens = torch.randint(3, 4096, (2, 40), generator=g)
+    targets = torch.roll(tokens, -1, dims=1)
+    targets[:, -1] = -1
+    targets[1, :7] = -1
+    with torch.inference_mode():
+        logits = model(tokens, targets)
+        loss = float(model.last_loss)
+    return ({"tokens": tokens.tolist(), "targets": targets.tolist(), "loss": loss, "rows_every": 5,
+             "torch": torch.__version__}, logits[:, ::5].numpy())
+
+
 SHIPPED = "tinyllamas_zh_story_q6w_qat_lr1e6"
 
 
@@ -272,6 +303,13 @@ def main():
         (HERE / "fp16_kv.json").write_text(json.dumps(doc, indent=1) + "\n")
         np.savez_compressed(HERE / "fp16_kv_logits.npz", rows=rows)
         print("sampling and FP16-KV fixtures written to", HERE)
+        return
+    if "--forward" in sys.argv:  # only the non-cached forward fixture
+        with tempfile.TemporaryDirectory() as d:
+            doc, rows = forward_all_request(Path(d))
+        (HERE / "forward_all.json").write_text(json.dumps(doc, indent=1) + "\n")
+        np.savez_compressed(HERE / "forward_all_logits.npz", rows=rows)
+        print("forward fixture written to", HERE)
         return
     (HERE / "codec.json").write_text(json.dumps(codec_vectors(), indent=1) + "\n")
     with tempfile.TemporaryDirectory() as d:

@@ -150,3 +150,22 @@ def test_oracle_fp16_kv_matches_reference_wrapper(tiny_files):
             if pos >= len(doc["prompt"]) - 1:
                 got.append(lg.numpy())
     assert np.array_equal(np.stack(got), rows)  # the same torch CPU operations: bit for bit
+
+
+def test_oracle_forward_all_matches_reference_forward(tiny_files):
+    """All-position logits and the masked loss of the reference's non-cached
+    forward (training/model.py:249-269; attention by scaled_dot_product_attention
+    there, by the cached step here: the same sums in another order)."""
+    import json
+
+    from conftest import GOLDEN
+    from oracle.model import forward_all
+
+    doc = json.loads((GOLDEN / "forward_all.json").read_text())
+    rows = np.load(GOLDEN / "forward_all_logits.npz")["rows"]
+    torch.set_num_threads(1)
+    orc = OracleModel.from_q6w(*tiny_files)
+    logits, loss = forward_all(orc, doc["tokens"], doc["targets"])
+    got = np.stack([lg[::doc["rows_every"]].numpy() for lg in logits])
+    assert np.abs(got - rows).max() <= 2e-5
+    assert loss == pytest.approx(doc["loss"], rel=1e-6)

@@ -1269,6 +1269,90 @@ __global__ void prefill_argmax_kernel(int n, const unsigned long long* __restric
   if (i < n) out[i] = argmax_index(keys[i]);
 }
 
+// Cross entropy of each token row against its target, as F.cross_entropy
+// with ignore_index=-1 (training/model.py:262): -(log_softmax(x)[t]) =
+// -((x[t] - max) - log(sum exp(x - max))).  One CTA per row (grid-stride);
+// a row whose target is -1, or that is invalid, counts 0; a target outside
+// [0, vocab) otherwise is flagged in err.
+__global__ void __launch_bounds__(256) row_nll_kernel(int rows, int vocab, const float* __restrict__ logits,
+                                                      const int32_t* __restrict__ targets, int stride,
+                                                      const int32_t* __restrict__ seq, const int32_t* __restrict__ pos,
+                                                      const int32_t* __restrict__ flags, float* __restrict__ nll,
+                                                      int32_t* __restrict__ counted, int32_t* err) {
+  __shared__ float red[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int t = targets[(int64_t)seq[r] * stride + pos[r]];
+    const bool in = !(flags[r] & SEQ_INVALID) && t != -1;
+    if (in && (t < 0 || t >= vocab)) {
+      if (threadIdx.x == 0) atomicOr(err, 1);
+    }
+    if (!in || t < 0 || t >= vocab) {
+      if (threadIdx.x == 0) {
+        nll[r] = 0.0f;
+        counted[r] = 0;
+      }
+      continue;
+    }
+    const float* x = logits + (int64_t)r * vocab;
+    float m = -INFINITY;
+    for (int c = threadIdx.x; c < vocab; c += blockDim.x) m = fmaxf(m, x[c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+    __syncthreads();
+    float s = 0.0f;
+    for (int c = threadIdx.x; c < vocab; c += blockDim.x) s += expf(__fsub_rn(x[c], m));
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = red[0];
+      for (int i = 1; i < 8; ++i) tot += red[i];
+      nll[r] = -__fsub_rn(__fsub_rn(x[t], m), logf(tot));
+      counted[r] = 1;
+    }
+    __syncthreads();
+  }
+}
+
+// Mean of the counted rows' cross entropies (FP64 sums, fixed order): the
+// reduction='mean' of F.cross_entropy; NaN when every target is ignored.
+__global__ void __launch_bounds__(256) mean_loss_kernel(int rows, const float* __restrict__ nll,
+                                                        const int32_t* __restrict__ counted, float* loss) {
+  __shared__ double rs[8];
+  __shared__ long long rc[8];
+  double s = 0.0;
+  long long c = 0;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    s += (double)nll[r];
+    c += counted[r];
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+  }
+  if (lane == 0) {
+    rs[warp] = s;
+    rc[warp] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0.0;
+    long long tc = 0;
+    for (int i = 0; i < 8; ++i) {
+      ts += rs[i];
+      tc += rc[i];
+    }
+    *loss = tc ? (float)(ts / (double)tc) : __int_as_float(0x7FC00000);
+  }
+}
+
 // ---- general tensor-core step (tcg.cuh) -------------------------------------
 
 // Shapes the general tensor-core linears handle: K (dim, hidden) multiples of
@@ -1991,6 +2075,63 @@ extern "C" int32_t q6w_prefill(const q6w_model* M, int32_t n_prompts, const int3
   if (last_argmax) {
     prefill_argmax_kernel<<<grid_for(n_prompts, 256), 256, 0, s>>>(n_prompts, w.keys, last_argmax);
     Q6W_LAUNCH_CHECK("prefill_argmax_kernel");
+  }
+  return Q6W_OK;
+}
+
+extern "C" int32_t q6w_forward_all(const q6w_model* M, int32_t n_prompts, const int32_t* prompts,
+                                   const int32_t* prompt_lens, int32_t prompt_stride, int32_t max_prompt_len,
+                                   int64_t total_tokens, float* k_cache, float* v_cache, int64_t cache_seq_stride,
+                                   float* logits, const int32_t* targets, float* loss, void* workspace,
+                                   size_t workspace_bytes, q6w_stream_t stream) {
+  clear_error();
+  if (!M) return fail(Q6W_ERR_ARG, "null model");
+  if (n_prompts < 0 || total_tokens < 0) return fail(Q6W_ERR_ARG, "n_prompts and total_tokens must be >= 0");
+  if (n_prompts == 0) return Q6W_OK;
+  if (total_tokens < n_prompts || total_tokens > kMaxPrefillRows)
+    return fail(Q6W_ERR_ARG, "total_tokens %lld must be in [n_prompts, %lld]", (long long)total_tokens,
+                (long long)kMaxPrefillRows);
+  if (!prompts || !prompt_lens || !logits) return fail(Q6W_ERR_ARG, "null prompts / prompt_lens / logits");
+  if ((targets == nullptr) != (loss == nullptr)) return fail(Q6W_ERR_ARG, "targets and loss go together");
+  if (max_prompt_len < 1 || max_prompt_len > M->d.max_seq_len || prompt_stride < max_prompt_len)
+    return fail(Q6W_ERR_ARG, "need 1 <= max_prompt_len <= max_seq_len (%d) and prompt_stride >= max_prompt_len",
+                M->d.max_seq_len);
+  if (!aligned(logits, 16) || M->d.vocab_size % 4) return fail(Q6W_ERR_ALIGN, "logits must be 16-byte aligned");
+  if (!workspace) return fail(Q6W_ERR_ARG, "null workspace");
+  if (!aligned(workspace, 256)) return fail(Q6W_ERR_ALIGN, "workspace must be 256-byte aligned");
+  const size_t need = prefill_layout(M, n_prompts, total_tokens, nullptr, nullptr, nullptr, nullptr);
+  if (workspace_bytes < need)
+    return fail(Q6W_ERR_ARG, "workspace of %zu bytes too small (%zu needed)", workspace_bytes, need);
+  int32_t st;
+  if ((st = check_cache(M, k_cache, v_cache, cache_seq_stride, n_prompts))) return st;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != M->device) return fail(Q6W_ERR_ARG, "model was created on device %d, current is %d", M->device, dev);
+  Work w;
+  int32_t *seq, *off;
+  prefill_layout(M, n_prompts, total_tokens, (char*)workspace, &w, &seq, &off);
+  const int rows = (int)total_tokens;
+  cudaStream_t s = (cudaStream_t)stream;
+  prefill_scan_kernel<<<1, 1024, 0, s>>>(n_prompts, prompt_lens, max_prompt_len, off, w.err);
+  Q6W_LAUNCH_CHECK("prefill_scan_kernel");
+  prefill_rows_kernel<<<n_prompts < 4096 ? n_prompts : 4096, 256, 0, s>>>(
+      n_prompts, rows, prompts, prompt_stride, prompt_lens, max_prompt_len, M->d.vocab_size, off, w, seq);
+  Q6W_LAUNCH_CHECK("prefill_rows_kernel");
+  w.seq = seq;
+  // every row through the layers and the vocab head (final RMSNorm + tied embedding): the logits of
+  // every position, row off[i] + j for position j of prompt i
+  EpiArgs v;
+  memset(&v, 0, sizeof(v));
+  v.y = logits;
+  v.ldy = M->d.vocab_size;
+  if ((st = enqueue_step(M, rows, w, k_cache, v_cache, cache_seq_stride, v, s, true))) return st;
+  if (targets) {
+    // per-row cross entropy into the (now unused) query buffer, row flags into gen
+    row_nll_kernel<<<rows < 8192 ? rows : 8192, 256, 0, s>>>(rows, M->d.vocab_size, logits, targets, prompt_stride,
+                                                             seq, w.pos, w.flags, w.qb, w.gen, w.err);
+    Q6W_LAUNCH_CHECK("row_nll_kernel");
+    mean_loss_kernel<<<1, 256, 0, s>>>(rows, w.qb, w.gen, loss);
+    Q6W_LAUNCH_CHECK("mean_loss_kernel");
   }
   return Q6W_OK;
 }

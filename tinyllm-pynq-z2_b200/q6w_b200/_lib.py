@@ -27,7 +27,7 @@ EXPORTS = (
     "q6w_forward_batch", "q6w_generate_greedy", "q6w_workspace_status", "q6w_linear_argmax",
     "q6w_rmsnorm", "q6w_gqa_attention", "q6w_linear_argmax_noalloc", "q6w_prefill_workspace_bytes",
     "q6w_prefill", "q6w_quantize_rows", "q6w_linear_workspace_bytes", "q6w_linear_ex", "q6w_generate",
-    "q6w_sample", "q6w_model_set_kv_dtype",
+    "q6w_sample", "q6w_model_set_kv_dtype", "q6w_forward_all",
 )
 
 
@@ -108,6 +108,8 @@ def _declare(lib):
                                                 c_int64, c_int64, S]),
         "q6w_rmsnorm": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, S]),
         "q6w_prefill_workspace_bytes": (c_size_t, [c_void_p, c_int32, c_int64]),
+        "q6w_forward_all": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p,
+                                      c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, S]),
         "q6w_prefill": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p,
                                   c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_size_t, S]),
         "q6w_gqa_attention": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,

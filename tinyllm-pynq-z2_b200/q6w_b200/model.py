@@ -291,6 +291,62 @@ class Q6WCudaTransformer:
         self.check_device_status(ws)
         return lg, caches
 
+    def forward_all(self, prompts, targets=None):
+        """Logits of every position of each prompt (a list of [len, vocab]
+        device tensors, views of one [sum(len), vocab] buffer) and, with
+        ``targets`` (a list of id lists of the same lengths, -1 = ignored),
+        the mean cross entropy as a device scalar -- the non-cached
+        ``Transformer.forward(tokens, targets)`` of training/model.py:249-269
+        on ragged prompts.  Returns (logits list, loss or None)."""
+        n = len(prompts)
+        lens = [len(p) for p in prompts]
+        if n == 0 or min(lens) < 1:
+            raise ValueError("every prompt needs at least one token")
+        if max(lens) > self.args.max_seq_len:
+            raise ValueError("Prompt exceeds the model context")
+        if targets is not None and [len(t) for t in targets] != lens:
+            raise ValueError("targets must have the prompts' lengths")
+        L, total = max(lens), sum(lens)
+        host = np.zeros((n, L), dtype=np.int32)
+        th = np.full((n, L), -1, dtype=np.int32)
+        for i, p in enumerate(prompts):
+            host[i, : len(p)] = p
+            if targets is not None:
+                th[i, : len(p)] = targets[i]
+        pr = torch.from_numpy(host).to(self.device)
+        ln = torch.tensor(lens, dtype=torch.int32, device=self.device)
+        tg = torch.from_numpy(th).to(self.device) if targets is not None else None
+        k, v = self.new_batch_cache(n)
+        logits = torch.empty((total, self.args.vocab_size), dtype=torch.float32, device=self.device)
+        loss = torch.empty(1, dtype=torch.float32, device=self.device) if targets is not None else None
+        ws, nbytes = self._prefill_workspace(n, total)
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.q6w_forward_all(
+                self._handle, n, pr.data_ptr(), ln.data_ptr(), L, L, total, k.data_ptr(), v.data_ptr(),
+                k[0].numel(), logits.data_ptr(), tg.data_ptr() if tg is not None else None,
+                loss.data_ptr() if loss is not None else None, ws.data_ptr(), nbytes, _lib.stream_handle()),
+                "q6w_forward_all")
+        self.check_device_status(ws)
+        return list(torch.split(logits, lens)), (loss[0] if loss is not None else None)
+
+    def forward(self, tokens, targets=None):
+        """``Transformer.forward`` of training/model.py:249-269 on a [B, T]
+        token batch: with ``targets`` ([B, T], -1 ignored) the logits of every
+        position [B, T, vocab] and ``self.last_loss`` = the mean cross
+        entropy; without, the last position's logits [B, 1, vocab] and
+        ``last_loss`` None."""
+        tok = torch.as_tensor(tokens)
+        if tok.dim() != 2:
+            raise ValueError("tokens must be [batch, seq_len]")
+        rows = tok.tolist()
+        if targets is None:
+            lg, _ = self.prefill_batch(rows)
+            self.last_loss = None
+            return lg[:, None, :]
+        lg, loss = self.forward_all(rows, torch.as_tensor(targets).tolist())
+        self.last_loss = loss
+        return torch.stack(lg)
+
     def generate_greedy_device(self, prompts, prompt_lens, max_prompt_len, new_tokens, stop_ids=(),
                                min_new_tokens=0, caches=None, keep_logits=False, prefill_event=None, sampling=None):
         """Device-resident generation (no host sync inside).
