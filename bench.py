@@ -42,10 +42,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--n-seqs", type=int, default=8192, help="sequences per GPU")
+    ap.add_argument("--n-seqs", type=int, default=8192,
+                    help="sequences per GPU (with --split: sequences of the whole job)")
+    ap.add_argument("--split", action="store_true",
+                    help="strong scaling: the --n-seqs sequences (and the 2048 prefill prompts) are divided "
+                         "across the GPUs instead of each GPU serving its own")
     ap.add_argument("--prompt-len", type=int, default=20)
     ap.add_argument("--new-tokens", type=int, default=128)
-    ap.add_argument("--cpu-sample-requests", type=int, default=2, help="requests per CPU worker per step")
+    ap.add_argument("--cpu-sample-requests", type=int, default=24,
+                    help="requests per CPU worker in the CPU baseline (about 10 s of CPU work each)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--verify-sample", type=int, default=512,
                     help="sequences of the timed output teacher-forced against the oracle (all ranks together)")
@@ -163,6 +168,96 @@ def verify_streams(bin_path, man_path, prompts, sampled, new_tokens, workers):
             "min_margin": min(r["min_margin"] for r in res)}
 
 
+def _cpu_prefill_worker(job):
+    """One single-thread process: the reference's prefill (the cached step over
+    every prompt token, torch_benchmark.py:263-264) on a few prompts."""
+    bin_path, man_path, prompts = job
+    import torch
+
+    torch.set_num_threads(1)
+    from oracle.model import OracleModel
+
+    m = OracleModel.from_q6w(bin_path, man_path)
+    t0 = time.perf_counter()
+    with torch.inference_mode():
+        for p in prompts:
+            k, v = m.new_cache()
+            for pos, tok in enumerate(p):
+                m.step(int(tok), pos, k, v)
+    return sum(len(p) for p in prompts), time.perf_counter() - t0
+
+
+def cpu_legs(bin_path, man_path, prompt, new_tokens):
+    """CPU baselines of the other configurations, on this host's cores, through
+    the oracle port of the reference's code path (bounded samples):
+    C1 -- B=1 generate (20-token prompt + 128 tokens) at 1 thread and all cores;
+    C3 -- the per-token prefill of a seeded 32-prompt subsample of the 2048
+          ragged prompts, one single-thread process per core, extrapolated to
+          all 2048 by prompt tokens;
+    C5 -- 8 decode steps of the 1.1B-shape config (FP32 weights: the same
+          cost as dequantized Q6W) after a 16-token prompt, all cores."""
+    import multiprocessing as mp
+
+    import numpy as np
+    import torch
+
+    from oracle.model import OracleArgs, OracleModel, greedy_request
+    from q6w_b200 import format as fmt
+
+    cores = cpu_cores()
+    out = {"cores": cores, "kind": "port"}
+    old = torch.get_num_threads()
+    orc = OracleModel.from_q6w(bin_path, man_path)
+    c1 = {}
+    for threads in (1, cores):
+        torch.set_num_threads(threads)
+        greedy_request(orc, prompt, 4)
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            greedy_request(orc, prompt, new_tokens)
+            ts.append(time.perf_counter() - t0)
+        c1[f"{threads}_threads_tok_s"] = round(new_tokens / statistics.median(ts), 1)
+    out["c1_b1_request"] = {**c1, "sample": f"median of 3 requests ({len(prompt)} + {new_tokens} tokens)"}
+    # C3: subsample of the bench's prefill prompts
+    rng = np.random.default_rng(2048)
+    lens_all = rng.integers(8, 257, 2048)
+    ids_all = rng.integers(3, 4096, (2048, 256)).astype(np.int32)
+    pick = np.random.default_rng(7).choice(2048, 32, replace=False)
+    prompts = [ids_all[i, : lens_all[i]].tolist() for i in pick]
+    jobs = [(str(bin_path), str(man_path), prompts[w::cores]) for w in range(min(cores, len(prompts)))]
+    with mp.get_context("spawn").Pool(len(jobs)) as pool:
+        res = pool.map(_cpu_prefill_worker, jobs)
+    toks = sum(r[0] for r in res)
+    busy = max(r[1] for r in res)
+    tok_s = toks / busy
+    out["c3_prefill"] = {"prefill_tok_s": round(tok_s, 1), "extrapolated_ms_for_2048_prompts":
+                         round(int(lens_all.sum()) / tok_s * 1e3, 1),
+                         "sample": f"32 of the 2048 prompts ({toks} tokens) over {len(jobs)} single-thread processes; "
+                                   "the 2048-prompt time is extrapolated by prompt tokens"}
+    # C5: 1.1B shape at all cores
+    torch.set_num_threads(cores)
+    args = OracleArgs.from_model_args(dict(fmt.SCALED_ARGS))
+    g = torch.Generator().manual_seed(3)
+    shapes = fmt._model_shapes(dict(fmt.SCALED_ARGS))
+    state = {k: (torch.randn(v, generator=g) * 0.02 if len(v) == 2 else torch.ones(v)) for k, v in shapes.items()}
+    state["output.weight"] = state["tok_embeddings.weight"]
+    big = OracleModel(args, state)
+    k, v = big.new_cache()
+    with torch.inference_mode():
+        for pos in range(16):
+            big.step(3 + pos, pos, k, v)
+        t0 = time.perf_counter()
+        for pos in range(16, 24):
+            big.step(5 + pos, pos, k, v)
+        sec = (time.perf_counter() - t0) / 8
+    del big, state, k, v
+    out["c5_b1_decode"] = {"ms_per_token": round(sec * 1e3, 2), "tok_s": round(1 / sec, 2),
+                           "sample": "8 decode steps after a 16-token prompt, all cores"}
+    torch.set_num_threads(old)
+    return out
+
+
 def run_reference(a):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -197,11 +292,15 @@ def run_reference(a):
 
 
 def workload_config(a, world):
+    split = getattr(a, "split", False)
+    per_gpu = -(-a.n_seqs // world) if split else a.n_seqs
+    where = f"{a.n_seqs} sequences split across {world} GPU(s)" if split else f"{a.n_seqs} sequences per GPU"
     return {"workload": (f"batched greedy decode, tiny Q6W model (dim 128, 5 layers, 8 q / 4 kv heads, hd 16, "
-                         f"hidden 384, vocab 4096, ctx 256): {a.n_seqs} sequences per GPU x ({a.prompt_len}-token "
+                         f"hidden 384, vocab 4096, ctx 256): {where} x ({a.prompt_len}-token "
                          f"prompt + {a.new_tokens} generated), FP32 KV cache"),
-            "sequences_per_gpu": a.n_seqs, "prompt_len": a.prompt_len, "new_tokens": a.new_tokens,
-            "global_sequences": a.n_seqs * world, "parallelism": f"dp{world} (independent replicas, no collectives)",
+            "sequences_per_gpu": per_gpu, "prompt_len": a.prompt_len, "new_tokens": a.new_tokens,
+            "global_sequences": a.n_seqs if split else a.n_seqs * world,
+            "parallelism": f"dp{world} (independent replicas, no collectives)",
             "l2": "inputs larger than L2: per-GPU KV cache 5.4 GB rewritten every step"}
 
 
@@ -282,8 +381,19 @@ def run_b200(a):
     tmp = tempfile.TemporaryDirectory()
     b, m = make_model_files(tmp.name)
     model = Q6WCudaTransformer.from_q6w(b, m, device=dev)
-    n, P, T = a.n_seqs, a.prompt_len, a.new_tokens
-    host_prompts = prompts_for(rank, n, P).pin_memory()
+    P, T = a.prompt_len, a.new_tokens
+    if a.split:
+        # one 8192-sequence job (prompts from one seed) divided across the ranks
+        from q6w_b200 import dp
+
+        lo, hi = dp.shard_range(a.n_seqs, rank, world)
+        host_prompts = prompts_for(0, a.n_seqs, P)[lo:hi].contiguous().pin_memory()
+        n = hi - lo
+        n_job = a.n_seqs
+    else:
+        n = a.n_seqs
+        host_prompts = prompts_for(rank, n, P).pin_memory()
+        n_job = n * world
     prompts = host_prompts.to(dev)
     lens = torch.full((n,), P, dtype=torch.int32, device=dev)
     caches = model.new_batch_cache(n)
@@ -354,7 +464,8 @@ def run_b200(a):
     b1 = b1_latency(model, host_prompts[0].tolist(), T, stream) if side else None
     gemv = scaled_gemv(dev, stream) if side else None
     sb1 = scaled_b1(dev, stream) if side else None
-    pf = prefill_c3(model, rank, world, stream) if side else None
+    # C3 prefill: at N=1, or in split mode on every rank (2048 prompts balanced by tokens, max over ranks)
+    pf = prefill_c3(model, rank, world, stream) if (side or (a.split and not a.only_main)) else None
     sweep = linear_sweep(dev, stream) if side else None
 
     t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -366,13 +477,13 @@ def run_b200(a):
         dist.all_reduce(cnt, op=dist.ReduceOp.SUM)
         dist.all_reduce(mm, op=dist.ReduceOp.MIN)
     ms, e2e_ms = float(t[0]), float(t[1])
-    parity = {"checked_sequences": int(cnt[0]), "of_sequences": n * world, "picks": int(cnt[1]),
+    parity = {"checked_sequences": int(cnt[0]), "of_sequences": n_job, "picks": int(cnt[1]),
               "exact": int(cnt[2]), "near_ties": int(cnt[3]), "failures": int(cnt[4]),
               "min_top1_top2_margin": round(float(mm[0]), 6),
               "method": "teacher-forced oracle (BatchScorer) over prompt + all generated tokens; a pick passes "
                         "if it is the oracle argmax or within 1e-4 of the oracle maximum",
               "rank0_first_failures": par["first_failures"], "rank0_seconds": par["seconds"]}
-    total_tokens = n * T * a.steps * world
+    total_tokens = n_job * T * a.steps
     value = total_tokens / (ms / 1e3)
     e2e_value = total_tokens / (e2e_ms / 1e3)
     launches_per_gen = 1 + (P + T - 1) * (1 + 5 * model.args.n_layers + 2)
@@ -380,7 +491,8 @@ def run_b200(a):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True,
+            "scaling": "strong" if a.split else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(a, world),
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(n * P * 4),
                     "d2h_bytes_per_step": int(n * T * 4)},
@@ -396,6 +508,7 @@ def run_b200(a):
                                     "sample": f"{cores} single-thread processes x {a.cpu_sample_requests} requests "
                                               f"({P}+{T} tokens, B=1 cached-step loop of the oracle port); "
                                               f"{toks} tokens in {busy:.1f} s"}
+            line["cpu_legs"] = cpu_legs(b, m, host_prompts[0].tolist(), T)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -677,6 +790,10 @@ def prefill_c3(model, rank, world, stream, reps=3):
         _, _, _, ws = model.prefill_batch_device(pr, ln, L, total, caches=caches)
     model.check_device_status(ws)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(reps):
@@ -684,11 +801,26 @@ def prefill_c3(model, rank, world, stream, reps=3):
     e1.record(stream)
     torch.cuda.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / reps
+    job_tokens = int(lens_all.sum())
+    if world > 1:
+        t = torch.tensor([sec], dtype=torch.float64, device=model.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t[0])
     del caches
     torch.cuda.empty_cache()
-    return {"workload": f"batched ragged prefill, tiny model: {len(mine)} of 2048 prompts, lengths U[8,256]",
-            "prompts": len(mine), "tokens": total, "ms": round(sec * 1e3, 3),
-            "prefill_tok_s": round(total / sec, 1), "prompts_s": round(len(mine) / sec, 1)}
+    # roofline: the linears of every prompt token (dim 128 model: 2 x 983,040 flop a token, issued three
+    # times as bf16 MMAs on the tensor cores), against the measured sustained bf16 peak
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    issued = 3 * 2 * 983_040 * job_tokens
+    return {"workload": f"batched ragged prefill, tiny model: 2048 prompts, lengths U[8,256], over {world} GPU(s) "
+                        f"balanced by tokens (this rank: {len(mine)} prompts, {total} tokens)",
+            "prompts": 2048, "tokens": job_tokens, "ms": round(sec * 1e3, 3),
+            "prefill_tok_s": round(job_tokens / sec, 1), "prompts_s": round(2048 / sec, 1),
+            "roofline": {"bound": "tensor", "achieved": round(issued / sec / 1e12, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(issued / sec / 1e12 / peak / world, 4),
+                         "work": "3 x 2 x 983,040 bf16 flop per prompt token (linears; attention and vocab excluded)",
+                         "peak_kind": "measured bf16_tflops_sustained per GPU"}}
 
 
 def scaled_b1(dev, stream, reps=3):

@@ -345,9 +345,20 @@ Q6W_API int32_t q6w_sample(const float* logits, int64_t ld, int32_t n, int32_t v
                            const q6w_sample_args* sampling, const int32_t* stop_ids, int32_t n_stop,
                            int32_t min_new_tokens, int32_t* tokens, q6w_stream_t stream);
 
-/* Synchronise `stream` and report device-side input errors recorded in the
- * workspace since the last call (then clear them): Q6W_OK or Q6W_ERR_DEVICE. */
+/* Synchronise `stream` and report device-side errors recorded in the
+ * workspace since the last call (then clear them): Q6W_OK, or Q6W_ERR_DEVICE
+ * for rejected input (bit 0) or a device wait that ran out of time (bit 2). */
 Q6W_API int32_t q6w_workspace_status(void* workspace, q6w_stream_t stream);
+
+/* Diagnostic with no counterpart in the reference: one CTA waits on an
+ * mbarrier that no thread arrives at, through the bounded-wait routine every
+ * pipeline wait of this library uses, limited to wait_cycles SM clock cycles
+ * (1 .. 2^31; the pipelines use about 4e9).  When the wait runs out the CTA
+ * sets the timeout bit in the workspace's error word and returns, so the
+ * context stays usable; q6w_workspace_status then reports Q6W_ERR_DEVICE.
+ * Lets a deployment check on its own GPU that a stalled pipeline ends with a
+ * status instead of a hang. */
+Q6W_API int32_t q6w_selftest_wait_timeout(void* workspace, int64_t wait_cycles, q6w_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -29,13 +29,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase; false if it did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait on an mbarrier phase: false if it did not complete within
+// `cycles` SM clock cycles.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t cycles) {
   const uint64_t t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
+    if (clock64() - t0 > cycles) return false;
   }
   return true;
+}
+
+// The pipelines' wait: bounded by kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitCycles);
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {

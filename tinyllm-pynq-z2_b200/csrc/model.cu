@@ -2300,8 +2300,34 @@ extern "C" int32_t q6w_workspace_status(void* workspace, q6w_stream_t stream) {
   if (flag) {
     Q6W_CUDA_TRY(cudaMemsetAsync(workspace, 0, sizeof(flag), s));
     Q6W_CUDA_TRY(cudaStreamSynchronize(s));
+    if (flag & tc::kErrTimeout)
+      return fail(Q6W_ERR_DEVICE, "a device-side wait ran out of time (error word 0x%x); the kernel stopped early",
+                  flag);
     return fail(Q6W_ERR_DEVICE, "a kernel rejected a token, position or prompt length (sequence skipped)");
   }
+  return Q6W_OK;
+}
+
+// One CTA waits on an mbarrier that no thread arrives at, through the
+// bounded-wait routine every pipeline wait uses, limited to `cycles`; when it
+// runs out the CTA records the timeout in the error word and returns.
+__global__ void selftest_wait_kernel(uint64_t cycles, int32_t* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait_for(&bar, 0, cycles)) atomicOr(err, tc::kErrTimeout);
+}
+
+extern "C" int32_t q6w_selftest_wait_timeout(void* workspace, int64_t wait_cycles, q6w_stream_t stream) {
+  clear_error();
+  if (!workspace || !aligned(workspace, 4)) return fail(Q6W_ERR_ARG, "q6w_selftest_wait_timeout: bad workspace");
+  if (wait_cycles < 1 || wait_cycles > (int64_t(1) << 31))
+    return fail(Q6W_ERR_ARG, "wait_cycles must be in [1, 2^31]");
+  selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((uint64_t)wait_cycles, static_cast<int32_t*>(workspace));
+  Q6W_LAUNCH_CHECK("selftest_wait_kernel");
   return Q6W_OK;
 }
 

@@ -27,7 +27,7 @@ EXPORTS = (
     "q6w_forward_batch", "q6w_generate_greedy", "q6w_workspace_status", "q6w_linear_argmax",
     "q6w_rmsnorm", "q6w_gqa_attention", "q6w_linear_argmax_noalloc", "q6w_prefill_workspace_bytes",
     "q6w_prefill", "q6w_quantize_rows", "q6w_linear_workspace_bytes", "q6w_linear_ex", "q6w_generate",
-    "q6w_sample", "q6w_model_set_kv_dtype", "q6w_forward_all",
+    "q6w_sample", "q6w_model_set_kv_dtype", "q6w_forward_all", "q6w_selftest_wait_timeout",
 )
 
 
@@ -102,6 +102,7 @@ def _declare(lib):
         "q6w_sample": (c_int32, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
                                  POINTER(SampleArgs), POINTER(c_int32), c_int32, c_int32, c_void_p, S]),
         "q6w_workspace_status": (c_int32, [c_void_p, S]),
+        "q6w_selftest_wait_timeout": (c_int32, [c_void_p, c_int64, S]),
         "q6w_linear_argmax": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                         c_int64, c_int64, c_int64, S]),
         "q6w_linear_argmax_noalloc": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
