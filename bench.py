@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
     ap.add_argument("--sweep-only", action="store_true", help="only run the isolated linear sweep and print it")
+    ap.add_argument("--profile", choices=("b1", "prefill", "sampler", "linear", "quantize"), default=None,
+                    help="only run one small case of that path a few times (for an ncu capture) and exit")
     ap.add_argument("--profile-scaled-step", type=int, nargs="?", const=1, default=None, metavar="N",
                     help="only run N short requests (2 + 3 tokens, default N=1) of the 1.1B-shape config and exit")
     return ap.parse_args()
@@ -923,6 +925,59 @@ def profile_gemv(shape):
     print(json.dumps({"profile_gemv": shape, "launches": 4, "y_abs_sum": float(y.abs().sum())}), flush=True)
 
 
+def profile_case(name):
+    """Small cases for ncu captures, each run 3 times after one warm-up:
+    b1 -- a B=1 request of the tiny model (20 + 128 tokens, the cluster kernel);
+    prefill -- 256 of the 2048 ragged prompts in one q6w_prefill;
+    sampler -- the sampler op on 8192 rows of 4096 logits (top-p 0.9, T 0.8);
+    linear -- the 4096 x 128 linear at N = 4096 on the tensor cores;
+    quantize -- the device writer on a 5632 x 2048 matrix."""
+    import numpy as np
+    import torch
+
+    from q6w_b200 import ops
+    from q6w_b200.model import Q6WCudaTransformer
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    tmp = tempfile.TemporaryDirectory()
+    if name in ("b1", "prefill"):
+        b, m = make_model_files(tmp.name)
+        model = Q6WCudaTransformer.from_q6w(b, m, device=dev)
+    if name == "b1":
+        pr = prompts_for(0, 1, 20).to(dev)
+        ln = torch.full((1,), 20, dtype=torch.int32, device=dev)
+        run = lambda: model.generate_greedy_device(pr, ln, 20, 128)
+    elif name == "prefill":
+        rng = np.random.default_rng(2048)
+        lens = rng.integers(8, 257, 2048)[:256].astype(np.int32)
+        ids = rng.integers(3, 4096, (2048, 256)).astype(np.int32)[:256]
+        pr, ln = torch.from_numpy(ids).to(dev), torch.from_numpy(lens).to(dev)
+        caches = model.new_batch_cache(256)
+        run = lambda: model.prefill_batch_device(pr, ln, 256, int(lens.sum()), caches=caches)
+    elif name == "sampler":
+        g = torch.Generator().manual_seed(1)
+        logits = (torch.randn(8192, 4096, generator=g) * 2).to(dev)
+        hist = torch.randint(0, 4096, (8192, 32), generator=g, dtype=torch.int32).to(dev)
+        hl = torch.full((8192,), 32, dtype=torch.int32, device=dev)
+        rng_state = torch.arange(1, 8193, dtype=torch.int64, device=dev)
+        run = lambda: ops.sample(logits, hist, hl, rng_state, 0.8, 0.9, repetition_penalty=1.1)
+    elif name == "linear":
+        rng = np.random.default_rng(4)
+        packed = torch.from_numpy(rng.integers(0, 256, 4096 * 96, dtype=np.uint8)).to(dev)
+        scales = torch.from_numpy(rng.uniform(0.001, 0.05, 4096).astype(np.float32)).to(dev)
+        x = torch.randn(4096, 128, device=dev)
+        run = lambda: ops.q6w_linear(x, packed, scales, 4096, 128)
+    else:
+        w = torch.randn(5632, 2048, device=dev) * 0.02
+        run = lambda: ops.quantize_rows(w)
+    for _ in range(4):
+        run()
+    torch.cuda.synchronize()
+    tmp.cleanup()
+    print(json.dumps({"profile": name, "launches_of_case": 4}), flush=True)
+
+
 def attention_roofline(model, caches, n, length, stream):
     """Time the decode-attention kernel alone (public op, one layer of this
     run's caches at the final length) and report its HBM roofline.
@@ -970,6 +1025,8 @@ def main():
     a = parse()
     if a.profile_gemv:
         profile_gemv(a.profile_gemv)
+    elif a.profile:
+        profile_case(a.profile)
     elif a.sweep_only:
         import torch
 

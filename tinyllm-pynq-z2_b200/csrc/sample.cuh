@@ -19,9 +19,10 @@
 // such values lie on the 2^-52 grid and their partial sums stay below 2, so
 // every FP64 sum of them is exact: the same in any order.  The crossing of a
 // running sum in descending order is then found by a radix select over the
-// float bit patterns (31 value bits in passes of 7 + 8 + 8 + 8 bits, a
-// histogram of FP64 sums per pass): the largest value v with
-// sum_{p >= v} p > T.  Equal values (a tie group) are taken in ascending
+// float bit patterns (the exponent, then the significand in passes of 8 + 8
+// + 7 bits, a histogram of exact fixed-point sums per pass): the largest
+// value v with sum_{p >= v} p > T.  The exponent pass is shared by the two
+// selections (the top-p crossing, then the coin's) and gives the kept total.  Equal values (a tie group) are taken in ascending
 // token order; the reference's unstable sort may order such a group
 // differently, which changes the pick only when it lands in the group.
 //
@@ -71,7 +72,7 @@ struct Args {
 };
 
 __host__ __device__ inline size_t smem_bytes(int vocab) {
-  return (size_t)vocab * 4 + (size_t)kMaxHistory * 4 + (size_t)(vocab + 31) / 32 * 4 + 256 * 12 + 1024;
+  return (size_t)vocab * 4 + (size_t)kMaxHistory * 4 + (size_t)(vocab + 31) / 32 * 4 + 256 * 28 + 1024;
 }
 
 __device__ __forceinline__ double warp_sum_d(double v) {
@@ -120,96 +121,197 @@ __device__ __forceinline__ float xorshift_coin(unsigned long long& s) {
   return (float)(uint32_t)(value >> 40) * (1.0f / 16777216.0f);  // (u32 >> 8) / 2^24, exact
 }
 
-// Largest candidate value v with sum_{cand p >= v} p > T, with G = the sum of
-// candidates above v and k = the 1-based position inside v's tie group where
-// the running sum first exceeds T.  Candidates: p >= cutoff.
-struct Sel {
-  float v;
-  double G;
-  int k;
-  double cum;  // G + k v
+// Exact sums of kept probabilities in 2^-52 fixed point.  A float32 p >= 2^-29
+// is an integer multiple of 2^-52 and the kept values sum to about 1, so
+// p * 2^52 and every sum of kept values are exact integers below 2^53: the
+// FP64 sums the reference forms, exact in any order.  Per histogram bin all
+// values share one exponent e, so a bin holds the integer sum S of their
+// 24-bit significands M (p = M * 2^(e - 150)) and its fixed-point sum is
+// S * 2^(e - 98).  S is accumulated as two 32-bit halves (sums of M >> 12 and
+// of M & 0xFFF, each below 2^27 for up to 32768 values) with native 32-bit
+// shared-memory atomics.  Below 2^-29 (a cutoff under 2^-29) the scaling
+// truncates, by less than 2^-52 a value.
+__device__ __forceinline__ unsigned long long fix52(float p) {
+  return (unsigned long long)((double)p * 4503599627370496.0);
+}
+// S > T for a fixed-point S  <=>  S > floor(T * 2^52)  (T * 2^52 is exact in FP64).
+__device__ __forceinline__ unsigned long long fix52_floor(double T) {
+  return (unsigned long long)floor(T * 4503599627370496.0);
+}
+__device__ __forceinline__ double unfix52(unsigned long long s) { return (double)s * (1.0 / 4503599627370496.0); }
+__device__ __forceinline__ unsigned long long scale_exp(unsigned long long S, int e) {
+  const int k = e - 98;
+  return k >= 0 ? (k < 64 ? S << k : 0ull) : (k > -64 ? S >> -k : 0ull);
+}
+
+// Shared histogram of one radix pass (256 bins) and the saved exponent pass.
+struct Hist {
+  uint32_t* hi;               // sum of M >> 12 per bin
+  uint32_t* lo;               // sum of M & 0xFFF per bin
+  int* cnt;                   // values per bin
+  unsigned long long* sum0;   // exponent pass: fixed-point sum per exponent
+  int* cnt0;
 };
 
-__device__ Sel radix_select(const float* p, int V, float cutoff, double T, double* hsum, int* hcnt, double* red) {
-  __shared__ uint32_t s_prefix, s_mask;
-  __shared__ double s_acc;
-  __shared__ int s_cnt;
-  __syncthreads();  // every thread has read the previous call's result
-  if (threadIdx.x == 0) {
-    s_prefix = 0u;
-    s_mask = 0u;
-    s_acc = 0.0;
+// One pass over the row: candidates (p >= cutoff) whose bits under mask equal
+// prefix, binned by (bits >> sh) & (nb - 1).  Strided over the threads (order
+// is free: the sums are exact).
+__device__ __forceinline__ void hist_pass(const float* p, int V, float cutoff, uint32_t prefix, uint32_t mask, int sh,
+                                          int nb, const Hist& h) {
+  for (int t = threadIdx.x; t < V; t += blockDim.x) {
+    const float v = p[t];
+    const uint32_t u = __float_as_uint(v);
+    if (!(v >= cutoff) || (u & mask) != prefix) continue;
+    const uint32_t m = (u & 0x7FFFFFu) | 0x800000u;
+    const int bin = (int)((u >> sh) & (uint32_t)(nb - 1));
+    atomicAdd(h.hi + bin, m >> 12);
+    atomicAdd(h.lo + bin, m & 0xFFFu);
+    atomicAdd(h.cnt + bin, 1);
   }
-  const int per = (V + blockDim.x - 1) / blockDim.x;
-  const int b0 = threadIdx.x * per, b1 = min(V, b0 + per);
-  const int shifts[4] = {24, 16, 8, 0}, widths[4] = {7, 8, 8, 8};
-  for (int pass = 0; pass < 4; ++pass) {
-    const int sh = shifts[pass], nb = 1 << widths[pass];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-      hsum[i] = 0.0;
-      hcnt[i] = 0;
+}
+
+__device__ __forceinline__ void hist_clear(const Hist& h) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    h.hi[i] = 0u;
+    h.lo[i] = 0u;
+    h.cnt[i] = 0;
+  }
+}
+
+// The exponent pass, shared by both selections: fixed-point sum and count of
+// the candidates per exponent; returns the total of the kept values (fixed
+// point) to every thread.
+__device__ unsigned long long exponent_pass(const float* p, int V, float cutoff, const Hist& h) {
+  __shared__ unsigned long long s_total;
+  hist_clear(h);
+  __syncthreads();
+  hist_pass(p, V, cutoff, 0u, 0u, 23, 256, h);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    unsigned long long part = 0ull;
+    for (int bin = threadIdx.x; bin < 256; bin += 32) {
+      const unsigned long long s = scale_exp(((unsigned long long)h.hi[bin] << 12) + h.lo[bin], bin);
+      h.sum0[bin] = s;
+      h.cnt0[bin] = h.cnt[bin];
+      part += s;
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (threadIdx.x == 0) s_total = part;
+  }
+  __syncthreads();
+  return s_total;
+}
+
+// Largest candidate value v with sum_{cand p >= v} p > T, with G = the sum of
+// candidates above v and k = the 1-based position inside v's tie group where
+// the running sum first exceeds T.  Candidates: p >= cutoff.  Tf =
+// fix52_floor(T); sums are fixed point.  Requires exponent_pass first.
+struct Sel {
+  float v;
+  unsigned long long G;
+  int k;
+  unsigned long long cum;  // G + k v
+};
+
+// Warp 0: walk the nb bins from the top, accumulating bin sums onto acc0, and
+// take the first bin where the running sum exceeds Tf.  lane l holds bins
+// nb-1-q*l .. nb-q(l+1) (q = nb / 32).
+template <typename BinSum>
+__device__ __forceinline__ void pick_bin(int nb, unsigned long long acc0, unsigned long long Tf, BinSum bin_sum,
+                                         int* chosen_out, unsigned long long* acc_out) {
+  const int lane = threadIdx.x & 31, q = nb / 32;
+  unsigned long long mine = 0ull;
+  for (int i = 0; i < q; ++i) mine += bin_sum(nb - 1 - q * lane - i);
+  unsigned long long incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const unsigned ball = __ballot_sync(0xffffffffu, acc0 + incl > Tf);
+  const int L = ball ? __ffs(ball) - 1 : 31;  // a crossing exists whenever Tf < the candidates' total
+  if (lane == L) {
+    unsigned long long acc = acc0 + incl - mine;
+    int chosen = nb - q * (L + 1);
+    for (int i = 0; i < q; ++i) {
+      const int bin = nb - 1 - q * L - i;
+      const unsigned long long s = bin_sum(bin);
+      if (acc + s > Tf) {
+        chosen = bin;
+        break;
+      }
+      acc += s;
+    }
+    *chosen_out = chosen;
+    *acc_out = acc;
+  }
+}
+
+__device__ Sel radix_select(const float* p, int V, float cutoff, unsigned long long Tf, const Hist& h) {
+  __shared__ uint32_t s_prefix, s_mask;
+  __shared__ unsigned long long s_acc;
+  __shared__ int s_cnt, s_bin;
+  __syncthreads();  // every thread has read the previous call's result
+  if (threadIdx.x < 32) {
+    pick_bin(256, 0ull, Tf, [&](int bin) { return h.sum0[bin]; }, &s_bin, &s_acc);
+    __syncwarp();
+    if (threadIdx.x == 0) {
+      s_cnt = h.cnt0[s_bin];
+      s_prefix = (uint32_t)s_bin << 23;
+      s_mask = 0xFFu << 23;
+    }
+  }
+  __syncthreads();
+  // significand bits 22..15, 14..7, 6..0 inside the chosen exponent
+  for (int pass = 0; pass < 3; ++pass) {
+    const int sh = pass < 2 ? 15 - 8 * pass : 0, nb = pass < 2 ? 256 : 128;
+    hist_clear(h);
     __syncthreads();
     const uint32_t prefix = s_prefix, mask = s_mask;
-    int cur = -1, cn = 0;
-    double cs = 0.0;
-    for (int t = b0; t < b1; ++t) {
-      const float v = p[t];
-      const uint32_t u = __float_as_uint(v);
-      if (!(v >= cutoff) || (u & mask) != prefix) continue;
-      const int bin = (int)((u >> sh) & (uint32_t)(nb - 1));
-      if (bin != cur) {
-        if (cur >= 0) {
-          atomicAdd(hsum + cur, cs);
-          atomicAdd(hcnt + cur, cn);
-        }
-        cur = bin;
-        cs = 0.0;
-        cn = 0;
-      }
-      cs += (double)v;
-      ++cn;
-    }
-    if (cur >= 0) {
-      atomicAdd(hsum + cur, cs);
-      atomicAdd(hcnt + cur, cn);
-    }
+    hist_pass(p, V, cutoff, prefix, mask, sh, nb, h);
     __syncthreads();
-    if (threadIdx.x == 0) {
-      double acc = s_acc;
-      int chosen = 0;
-      for (int bin = nb - 1; bin >= 0; --bin) {
-        if (acc + hsum[bin] > T) {
-          chosen = bin;
-          break;
-        }
-        acc += hsum[bin];
+    if (threadIdx.x < 32) {
+      const int e = (int)(prefix >> 23);
+      pick_bin(nb, s_acc, Tf,
+               [&](int bin) { return scale_exp(((unsigned long long)h.hi[bin] << 12) + h.lo[bin], e); }, &s_bin,
+               &s_acc);
+      __syncwarp();
+      if (threadIdx.x == 0) {
+        s_cnt = h.cnt[s_bin];
+        s_prefix = prefix | ((uint32_t)s_bin << sh);
+        s_mask = mask | ((uint32_t)(nb - 1) << sh);
       }
-      s_acc = acc;
-      s_cnt = hcnt[chosen];
-      s_prefix = prefix | ((uint32_t)chosen << sh);
-      s_mask = mask | ((uint32_t)(nb - 1) << sh);
     }
     __syncthreads();
   }
   Sel r;
   r.v = __uint_as_float(s_prefix);
   r.G = s_acc;
-  double s = r.G;
+  const unsigned long long vf = fix52(r.v);
+  unsigned long long s = r.G;
   int k = 0;
   const int cnt = s_cnt;
   do {
-    s += (double)r.v;
+    s += vf;
     ++k;
-  } while (s <= T && k < cnt);
+  } while (s <= Tf && k < cnt);
   r.k = k;
   r.cum = s;
-  (void)red;
   return r;
 }
 
 // Index of the k-th (1-based) token, in ascending order, whose value equals v.
 __device__ int kth_equal(const float* p, int V, float v, int k, double* red, int* ired) {
+  if (k == 1) {  // the usual case: the first equal value
+    int found = 0x7fffffff;
+    for (int t = threadIdx.x; t < V; t += blockDim.x)
+      if (p[t] == v) {
+        found = t;
+        break;
+      }
+    return block_reduce<int>(found, ired, [](int a, int b) { return a < b ? a : b; });
+  }
   const int per = (V + blockDim.x - 1) / blockDim.x;
   const int b0 = threadIdx.x * per, b1 = min(V, b0 + per);
   int c = 0;
@@ -239,9 +341,13 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(Args a) {
   float* l = reinterpret_cast<float*>(sm_raw);
   int32_t* hist = reinterpret_cast<int32_t*>(sm_raw + (size_t)V * 4);
   uint32_t* ban = reinterpret_cast<uint32_t*>(sm_raw + (size_t)V * 4 + (size_t)kMaxHistory * 4);
-  double* hsum = reinterpret_cast<double*>(sm_raw + (size_t)V * 4 + (size_t)kMaxHistory * 4 +
-                                           ((size_t)(V + 31) / 32 * 4 + 7) / 8 * 8);
-  int* hcnt = reinterpret_cast<int*>(hsum + 256);
+  Hist h;
+  h.sum0 = reinterpret_cast<unsigned long long*>(sm_raw + (size_t)V * 4 + (size_t)kMaxHistory * 4 +
+                                                  ((size_t)(V + 31) / 32 * 4 + 7) / 8 * 8);
+  h.hi = reinterpret_cast<uint32_t*>(h.sum0 + 256);
+  h.lo = h.hi + 256;
+  h.cnt = reinterpret_cast<int*>(h.lo + 256);
+  h.cnt0 = h.cnt + 256;
   const Params& P = a.p;
   const int g = a.hist_len[b];
   const int gh = g < kMaxHistory ? g : kMaxHistory;
@@ -252,14 +358,17 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(Args a) {
 
   // ---- repetition penalty on each distinct generated token (torch_benchmark.py:188-198)
   if (P.repetition_penalty != 1.0f && gh > 0) {
+    // once per distinct token: the thread that sets the token's bit applies it
+    const int words = (V + 31) / 32;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) ban[i] = 0u;
+    __syncthreads();
     for (int i = threadIdx.x; i < gh; i += blockDim.x) {
       const int t = hist[i];
-      bool first = t >= 0 && t < V;
-      for (int j = 0; j < i && first; ++j) first = hist[j] != t;
-      if (first) {
-        const float v = l[t];
-        l[t] = v < 0.0f ? __fmul_rn(v, P.repetition_penalty) : __fdiv_rn(v, P.repetition_penalty);
-      }
+      if (t < 0 || t >= V) continue;
+      const uint32_t bit = 1u << (t & 31);
+      if (atomicOr(ban + (t >> 5), bit) & bit) continue;
+      const float v = l[t];
+      l[t] = v < 0.0f ? __fmul_rn(v, P.repetition_penalty) : __fdiv_rn(v, P.repetition_penalty);
     }
     __syncthreads();
   }
@@ -369,18 +478,16 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(Args a) {
       found = block_reduce<int>(found, redi, [](int x, int y) { return x < y ? x : y; });
       token = found == 0x7fffffff ? V - 1 : found;
     } else {
-      double tot = 0.0;
-      for (int t = b0; t < b1; ++t)
-        if (l[t] >= P.cutoff) tot += (double)l[t];
-      tot = block_reduce<double>(tot, redd, [](double x, double y) { return x + y; });
+      const unsigned long long tot = exponent_pass(l, V, P.cutoff, h);
+      const unsigned long long top = fix52_floor(P.top_p);
       double cum_last;
-      if (tot > P.top_p) {
-        cum_last = radix_select(l, V, P.cutoff, P.top_p, hsum, hcnt, redd).cum;
+      if (tot > top) {
+        cum_last = unfix52(radix_select(l, V, P.cutoff, top, h).cum);
       } else {
-        cum_last = tot;  // the whole kept list (the reference's last_index = len - 1)
+        cum_last = unfix52(tot);  // the whole kept list (the reference's last_index = len - 1)
       }
       const double target = coin * cum_last;
-      const Sel s = radix_select(l, V, P.cutoff, target, hsum, hcnt, redd);
+      const Sel s = radix_select(l, V, P.cutoff, fix52_floor(target), h);
       token = kth_equal(l, V, s.v, s.k, redd, redi);
       if (token == 0x7fffffff) token = V - 1;  // not reached: the select always lands on a kept value
     }
