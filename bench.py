@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
     ap.add_argument("--sweep-only", action="store_true", help="only run the isolated linear sweep and print it")
-    ap.add_argument("--profile", choices=("b1", "prefill", "sampler", "linear", "quantize"), default=None,
+    ap.add_argument("--profile", choices=("b1", "prefill", "prefill_full", "sampler", "linear", "quantize"), default=None,
                     help="only run one small case of that path a few times (for an ncu capture) and exit")
     ap.add_argument("--profile-scaled-step", type=int, nargs="?", const=1, default=None, metavar="N",
                     help="only run N short requests (2 + 3 tokens, default N=1) of the 1.1B-shape config and exit")
@@ -489,6 +489,16 @@ def run_b200(a):
     value = total_tokens / (ms / 1e3)
     e2e_value = total_tokens / (e2e_ms / 1e3)
     launches_per_gen = 1 + (P + T - 1) * (1 + 5 * model.args.n_layers + 2)
+    # whole-generation HBM floor: K/V rows read by attention at lengths 1..P+T-1 plus the rows written
+    kvb = 2 * model.n_kv_heads * model.head_dim * 4 * model.args.n_layers
+    steps_gen = P + T - 1
+    gen_bytes = n_job * kvb * (steps_gen * (steps_gen + 1) // 2 + steps_gen)
+    peak_hbm, _ = measured_peaks()
+    step_hbm = {"kv_bytes_per_generation": gen_bytes,
+                "achieved_gbs": round(gen_bytes * a.steps / (ms / 1e3) / world / 1e9, 1),
+                "frac": round(gen_bytes * a.steps / (ms / 1e3) / world / 1e9 / peak_hbm, 4),
+                "note": "K/V cache bytes a generation must move (reads at every length + writes) over the "
+                        "whole timed step, per GPU"}
 
     if rank == 0:
         line = {
@@ -499,7 +509,8 @@ def run_b200(a):
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": int(n * P * 4),
                     "d2h_bytes_per_step": int(n * T * 4)},
             "gpu_launches": launches_per_gen * a.steps,
-            "roofline": roof, "clocks": clocks, "all_sequences_full_length": ok_len, "parity": parity,
+            "roofline": roof, "step_hbm": step_hbm, "clocks": clocks, "all_sequences_full_length": ok_len,
+            "parity": parity,
             "b1": b1, "gemv_scaled": gemv, "scaled_b1": sb1, "prefill": pf, "linear_sweep": sweep,
         }
         if not a.no_cpu_baseline and not a.only_main and world == 1:
@@ -929,6 +940,7 @@ def profile_case(name):
     """Small cases for ncu captures, each run 3 times after one warm-up:
     b1 -- a B=1 request of the tiny model (20 + 128 tokens, the cluster kernel);
     prefill -- 256 of the 2048 ragged prompts in one q6w_prefill;
+    prefill_full -- all 2048 ragged prompts (lengths U[8, 256]) in one q6w_prefill;
     sampler -- the sampler op on 8192 rows of 4096 logits (top-p 0.9, T 0.8);
     linear -- the 4096 x 128 linear at N = 4096 on the tensor cores;
     quantize -- the device writer on a 5632 x 2048 matrix."""
@@ -941,7 +953,7 @@ def profile_case(name):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     tmp = tempfile.TemporaryDirectory()
-    if name in ("b1", "prefill"):
+    if name in ("b1", "prefill", "prefill_full"):
         b, m = make_model_files(tmp.name)
         model = Q6WCudaTransformer.from_q6w(b, m, device=dev)
     if name == "b1":
@@ -954,6 +966,13 @@ def profile_case(name):
         ids = rng.integers(3, 4096, (2048, 256)).astype(np.int32)[:256]
         pr, ln = torch.from_numpy(ids).to(dev), torch.from_numpy(lens).to(dev)
         caches = model.new_batch_cache(256)
+        run = lambda: model.prefill_batch_device(pr, ln, 256, int(lens.sum()), caches=caches)
+    elif name == "prefill_full":
+        rng = np.random.default_rng(2048)
+        lens = rng.integers(8, 257, 2048).astype(np.int32)
+        ids = rng.integers(3, 4096, (2048, 256)).astype(np.int32)
+        pr, ln = torch.from_numpy(ids).to(dev), torch.from_numpy(lens).to(dev)
+        caches = model.new_batch_cache(2048)
         run = lambda: model.prefill_batch_device(pr, ln, 256, int(lens.sum()), caches=caches)
     elif name == "sampler":
         g = torch.Generator().manual_seed(1)
@@ -1009,6 +1028,21 @@ def attention_roofline(model, caches, n, length, stream):
     nbytes = 2 * n * length * KV * hd * 4 + 2 * n * H * hd * 4
     peak, kind = measured_peaks()
     ach = nbytes / sec / 1e9
+    # over the generation: every 8th attention length 1..length, each weighted as one step (bytes and
+    # times summed, so the fraction is the one the whole generation's attention launches reach)
+    tb = tt = 0.0
+    for ln in sorted(set(list(range(1, length + 1, 8)) + [length])):
+        lens.fill_(ln)
+        ops.gqa_attention(q, kl, vl, lens, H // KV)
+        e0.record(stream)
+        for _ in range(5):
+            ops.gqa_attention(q, kl, vl, lens, H // KV)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tt += e0.elapsed_time(e1) / 1e3 / 5
+        tb += 2 * n * ln * KV * hd * 4 + 2 * n * H * hd * 4
+    over = {"lengths": f"1..{length} every 8th (and {length})", "achieved": round(tb / tt / 1e9, 1),
+            "frac": round(tb / tt / 1e9 / peak, 4)}
     # DRAM bytes (read + written) of one launch as ncu measured them on a smaller capture of the same
     # kernel: 2048 sequences at length 147 moved 159.89 MB; traffic grows with the sequence count
     ncu_bytes, ncu_seqs, ncu_len = 159.89e6, 2048, 147
@@ -1018,7 +1052,7 @@ def attention_roofline(model, caches, n, length, stream):
             "peak_kind": f"{kind} hbm_gbs (copy, burst)", "traffic": traffic,
             "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at {ncu_seqs} "
                                f"sequences, length {ncu_len}, scaled by sequences ({n})") if traffic else None,
-            "bytes_per_launch": nbytes, "us_per_launch": round(sec * 1e6, 2)}
+            "bytes_per_launch": nbytes, "us_per_launch": round(sec * 1e6, 2), "over_generation": over}
 
 
 def main():

@@ -1,0 +1,75 @@
+"""GPU: launch-mode variants of the batched paths.
+
+* The prefill's causal attention (attn_prompt_kernel: one CTA per prompt,
+  KV head and block of query rows, keys staged through shared memory once)
+  is the kernel that runs for the head layouts it covers, and agrees with the
+  decode step's attention on the same prompts to rounding: the logits of the
+  last prompt position within the step tests' 2e-4, the layer-0 K/V rows bit
+  for bit (the same QKV epilogue on the same embeddings), later layers within
+  1e-4.
+* Programmatic dependent launch across the tensor-core step (opt-in with
+  Q6W_PDL=1 at model creation) changes only when kernels start: generated
+  tokens, step logits and caches are bit-identical to the default launches.
+"""
+
+import os
+
+import pytest
+import torch
+from torch.profiler import ProfilerActivity, profile
+
+from q6w_b200.model import Q6WCudaTransformer
+
+pytestmark = pytest.mark.gpu
+
+
+def _kernels(fn):
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+def _prompts(n, seed, lo, hi, vocab):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(lo, hi + 1, (n,), generator=g).tolist()
+    return [torch.randint(3, vocab, (L,), generator=g).tolist() for L in lens]
+
+
+@pytest.fixture(scope="module")
+def tiny(tiny_files):
+    return Q6WCudaTransformer.from_q6w(*tiny_files)
+
+
+def test_prefill_runs_prompt_attention_and_matches_step_path(tiny):
+    prompts = _prompts(80, 31, 1, 150, 4096)
+    names = _kernels(lambda: tiny.prefill_batch(prompts))
+    assert any("attn_prompt_kernel" in n for n in names), names
+    assert not any("attn_warp_kernel" in n for n in names)
+    lg, (k, v) = tiny.prefill_batch(prompts)
+    # the decode step path over the same prompts (one position per step, per-row attention)
+    res = tiny.generate_greedy(prompts, 1, keep_logits=True)
+    step_lg = res.logits[:, 0]
+    assert float((lg - step_lg).abs().max()) <= 2e-4
+    kg, vg = res.caches
+    for i, p in enumerate(prompts):
+        L = len(p)
+        # layer 0 comes from the embeddings through the same QKV epilogue; later layers see the
+        # attention outputs, which round differently between the two kernels
+        assert torch.equal(k[i, 0, :L], kg[i, 0, :L]) and torch.equal(v[i, 0, :L], vg[i, 0, :L]), i
+        assert float((k[i, :, :L] - kg[i, :, :L]).abs().max()) <= 1e-4, i
+        assert float((v[i, :, :L] - vg[i, :, :L]).abs().max()) <= 1e-4, i
+
+
+def test_pdl_step_bit_identical(tiny_files, tiny):
+    os.environ["Q6W_PDL"] = "1"
+    try:
+        fast = Q6WCudaTransformer.from_q6w(*tiny_files)
+    finally:
+        del os.environ["Q6W_PDL"]
+    prompts = _prompts(300, 32, 4, 24, 4096)
+    a = fast.generate_greedy(prompts, 12, keep_logits=True)
+    b = tiny.generate_greedy(prompts, 12, keep_logits=True)
+    assert a.sampled == b.sampled
+    assert torch.equal(a.logits, b.logits)
+    assert torch.equal(a.caches[0], b.caches[0]) and torch.equal(a.caches[1], b.caches[1])

@@ -23,6 +23,7 @@
 
 #include <mutex>
 #include <new>
+#include <utility>
 #include <vector>
 
 #include "b1.cuh"
@@ -55,6 +56,10 @@ struct Work {
   float* logits;       // sampling: the step's logits [N, vocab] (null unless laid out for sampling)
   unsigned long long* rng;  // sampling: XorShift64 state per sequence
   uint32_t* sync;      // persistent B=1 step: grid-barrier arrivals and the abort word
+  const int32_t* poff;   // prefill: row offset and length of every prompt (null otherwise)
+  const int32_t* plens;
+  int32_t n_prompts, max_len;
+  int32_t pdl;           // launch the tensor-core step's kernels with programmatic dependencies
 };
 
 struct GraphKey {
@@ -83,6 +88,7 @@ struct q6w_model {
   bool use_b1 = false;  // shapes qualify for the single-request cluster kernel
   bool kv_half = false; // the KV cache holds FP16 (q6w_model_set_kv_dtype)
   bool use_pdec = false;  // shapes qualify for the persistent B=1 step (pdec.cuh)
+  bool use_pdl = false;   // programmatic dependent launch in the tensor-core step (opt-in: Q6W_PDL=1)
   int pdec_grid = 0;
   size_t pdec_smem = 0;
   size_t b1_smem = 0;
@@ -94,6 +100,24 @@ static size_t carve(char*& p, size_t bytes) {
   size_t off = (size_t)p;
   p += (bytes + 255) & ~(size_t)255;
   return off;
+}
+
+// Launch with an optional programmatic dependency on the stream's preceding
+// kernel (the kernel itself calls grid_dep_wait before reading its inputs).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // Workspace of N sequences.  With `sample`, the sampler's regions (the step
@@ -123,6 +147,9 @@ static size_t layout(const q6w_model* M, int N, char* base, Work* w, bool sample
     t.xs_img = t.att_img = t.hs_img = nullptr;
   }
   t.seq = nullptr;
+  t.poff = t.plens = nullptr;
+  t.n_prompts = t.max_len = 0;
+  t.pdl = 0;
   t.logits = nullptr;
   t.rng = nullptr;
   if (sample) {
@@ -640,6 +667,8 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
   constexpr int PPW = 32 / R;
   constexpr int ROW = KV * HD;  // floats per cached row
   static_assert(32 % R == 0, "a row must map onto a power-of-two lane group");
+  grid_dep_launch();
+  grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= n) return;
@@ -764,38 +793,175 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
   }
 }
 
+// Causal attention of the token rows of a batched prefill (rows of prompt p
+// are off[p] .. off[p] + len[p] - 1, row j at position j; torch_benchmark.py's
+// per-position step over the prompt, :263-264).  A CTA takes one prompt, one
+// KV head and a block of kRB query rows; the keys its rows need (positions
+// 0 .. last row) pass through shared memory once, in tiles of kPT positions,
+// instead of once per row.  Thread = (query row, q head of the group): q and
+// the output accumulator in registers, keys read as shared-memory broadcasts.
+// Per key the arithmetic is the decode kernel's (dot as 16-element FMA chains
+// per chunk added pairwise, score = dot / denom, online softmax with expf,
+// output acc / l); keys are taken in position order, so results agree with
+// the decode path to rounding (not bit for bit: the decode kernel splits keys
+// over lane groups).  Two keys go through the dot products at once, as
+// packed FP32x2 FMAs.
+constexpr int kPromptThreads = 128;
+constexpr int kPT = 64;  // key positions per shared-memory tile
+
+template <int HD, int REP, bool SPLIT, typename KT = float>
+__global__ void __launch_bounds__(kPromptThreads) attn_prompt_kernel(
+    const float* __restrict__ qb, int ldq, const KT* __restrict__ kc, const KT* __restrict__ vc, int64_t cstride,
+    int64_t layer_off, const int32_t* __restrict__ off, const int32_t* __restrict__ lens, int max_len, int KV,
+    int64_t rows, const int32_t* __restrict__ flags, float denom, float* __restrict__ out, int ldo,
+    uint8_t* __restrict__ out_img) {
+  constexpr int kRB = kPromptThreads / REP;  // query rows per CTA
+  constexpr int C = HD / 16;
+  __shared__ __align__(16) float sk[kPT * HD];
+  __shared__ __align__(16) float sv[kPT * HD];
+  grid_dep_launch();
+  grid_dep_wait();
+  const int blocks = (max_len + kRB - 1) / kRB;
+  const int p = blockIdx.x / blocks, r0 = (blockIdx.x % blocks) * kRB;
+  const int g = blockIdx.y;
+  const int L = lens[p];
+  if (L < 1 || L > max_len || r0 >= L) return;  // block-uniform
+  const int j = threadIdx.x / kRB;
+  const int i = r0 + threadIdx.x % kRB;  // position of this thread's query row
+  const int64_t row = (int64_t)off[p] + i;
+  const bool inside = i < L && row < rows;  // a total shorter than the lengths (flagged) ends the rows
+  const bool act = inside && !(flags[row] & SEQ_INVALID);
+  const int K = KV * REP * HD;
+  const int h = g * REP + j;
+  float q[HD];
+#pragma unroll
+  for (int c = 0; c < HD; ++c) q[c] = 0.0f;
+  if (act) {
+    const float4* qp = reinterpret_cast<const float4*>(qb + row * ldq + h * HD);
+#pragma unroll
+    for (int c = 0; c < HD / 4; ++c) {
+      const float4 v = qp[c];
+      q[4 * c] = v.x; q[4 * c + 1] = v.y; q[4 * c + 2] = v.z; q[4 * c + 3] = v.w;
+    }
+  }
+  float2 acc[HD / 2];
+#pragma unroll
+  for (int c = 0; c < HD / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
+  float m = -INFINITY, l = 0.0f;
+  const bool pow2 = denom > 0.0f && __float_as_uint(denom) << 9 == 0u;  // x / 2^e == x * 2^-e exactly
+  const float inv = pow2 ? 1.0f / denom : 0.0f;
+  const int kend = min(L, r0 + kRB);  // keys the block needs
+  const int64_t ROW = (int64_t)KV * HD;
+  const KT* kb = kc + (int64_t)p * cstride + layer_off + g * HD;
+  const KT* vb = vc + (int64_t)p * cstride + layer_off + g * HD;
+  for (int t0 = 0; t0 < kend; t0 += kPT) {
+    const int tn = min(kPT, kend - t0);
+    __syncthreads();  // the previous tile is consumed
+    for (int e = threadIdx.x; e < tn * (HD / 4); e += kPromptThreads) {
+      const int t = e / (HD / 4), c4 = e % (HD / 4);
+      reinterpret_cast<float4*>(sk)[e] = load_kv4(kb + (t0 + t) * ROW + 4 * c4);
+      reinterpret_cast<float4*>(sv)[e] = load_kv4(vb + (t0 + t) * ROW + 4 * c4);
+    }
+    __syncthreads();
+    const int mine = act ? min(tn, i + 1 - t0) : 0;  // keys <= i in this tile
+    for (int tt = 0; tt < mine; tt += 2) {
+      const bool two = tt + 1 < mine;
+      const float* k0 = sk + tt * HD;
+      const float* k1 = two ? k0 + HD : k0;
+      float2 dc[C];
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        float2 d = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < 16; u += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(k0 + 16 * c + u);
+          const float4 b = *reinterpret_cast<const float4*>(k1 + 16 * c + u);
+          d = __ffma2_rn(make_float2(q[16 * c + u], q[16 * c + u]), make_float2(a.x, b.x), d);
+          d = __ffma2_rn(make_float2(q[16 * c + u + 1], q[16 * c + u + 1]), make_float2(a.y, b.y), d);
+          d = __ffma2_rn(make_float2(q[16 * c + u + 2], q[16 * c + u + 2]), make_float2(a.z, b.z), d);
+          d = __ffma2_rn(make_float2(q[16 * c + u + 3], q[16 * c + u + 3]), make_float2(a.w, b.w), d);
+        }
+        dc[c] = d;
+      }
+#pragma unroll
+      for (int w = 1; w < C; w <<= 1)  // the decode kernel's butterfly order
+#pragma unroll
+        for (int c = 0; c < C; c += 2 * w) dc[c] = __fadd2_rn(dc[c], dc[c + w]);
+      const float d2[2] = {dc[0].x, dc[0].y};
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        if (s == 1 && !two) break;
+        const float sc = pow2 ? d2[s] * inv : __fdiv_rn(d2[s], denom);
+        if (sc > m) {
+          const float cf = expf(m - sc);
+          l *= cf;
+#pragma unroll
+          for (int c = 0; c < HD / 2; ++c) acc[c] = __fmul2_rn(acc[c], make_float2(cf, cf));
+          m = sc;
+        }
+        const float pr = expf(sc - m);
+        l += pr;
+        const float* vr = sv + (tt + s) * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 4; ++c) {
+          const float4 v = *reinterpret_cast<const float4*>(vr + 4 * c);
+          acc[2 * c] = __ffma2_rn(make_float2(pr, pr), make_float2(v.x, v.y), acc[2 * c]);
+          acc[2 * c + 1] = __ffma2_rn(make_float2(pr, pr), make_float2(v.z, v.w), acc[2 * c + 1]);
+        }
+      }
+    }
+  }
+  if (!inside) return;
+  float o[HD];
+#pragma unroll
+  for (int c = 0; c < HD / 2; ++c) {
+    o[2 * c] = act ? __fdiv_rn(acc[c].x, l) : 0.0f;
+    o[2 * c + 1] = act ? __fdiv_rn(acc[c].y, l) : 0.0f;
+  }
+  if (SPLIT) {
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c) {
+      const float o8[8] = {o[8 * c], o[8 * c + 1], o[8 * c + 2], o[8 * c + 3],
+                           o[8 * c + 4], o[8 * c + 5], o[8 * c + 6], o[8 * c + 7]};
+      tc::img_store8(out_img, row, h * HD + 8 * c, K, o8);
+    }
+  } else {
+    float4* op = reinterpret_cast<float4*>(out + row * ldo + h * HD);
+#pragma unroll
+    for (int c = 0; c < HD / 4; ++c) op[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+  }
+}
+
 // Launch the streaming kernel when the shape has an instantiation; returns
 // false to fall back to the per-head kernel.
 static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st, const float* qb, int ldq,
                              const void* kc, const void* vc, int64_t cstride, int64_t layer_off,
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo,
                              int S, float denom, uint8_t* out_img = nullptr, const int32_t* seq = nullptr,
-                             bool kv_half = false) {
+                             bool kv_half = false, bool pdl = false) {
+  cudaError_t e = cudaSuccess;  // a launch error is read by the caller's launch check
   const float* kf = static_cast<const float*>(kc);
   const float* vf = static_cast<const float*>(vc);
   const __half* kh = static_cast<const __half*>(kc);
   const __half* vh = static_cast<const __half*>(vc);
 #define Q6W_ROWS(HDV, KVV, REPV)                                                                           \
   if (hd == HDV && KV == KVV && rep == REPV) {                                                             \
-    const int nb = ((int)grid.x + 3) / 4;                                                                  \
+    const dim3 nb(((int)grid.x + 3) / 4), bl(128);                                                         \
     if (kv_half && out_img)                                                                                \
-      attn_warp_kernel<HDV, KVV, REPV, true, __half><<<nb, 128, 0, st>>>(qb, ldq, kh, vh, cstride,         \
-                                                                         layer_off, len, len_add, flags,   \
-                                                                         out, ldo, S, denom, (int)grid.x,  \
-                                                                         out_img, seq);                    \
+      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, true, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,    \
+                   cstride, layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, out_img, seq); \
     else if (kv_half)                                                                                      \
-      attn_warp_kernel<HDV, KVV, REPV, false, __half><<<nb, 128, 0, st>>>(qb, ldq, kh, vh, cstride,        \
-                                                                          layer_off, len, len_add, flags,  \
-                                                                          out, ldo, S, denom, (int)grid.x, \
-                                                                          nullptr, seq);                   \
+      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, false, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,   \
+                   cstride, layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x,               \
+                   (uint8_t*)nullptr, seq);                                                                \
     else if (out_img)                                                                                      \
-      attn_warp_kernel<HDV, KVV, REPV, true><<<nb, 128, 0, st>>>(qb, ldq, kf, vf, cstride, layer_off,      \
-                                                                 len, len_add, flags, out, ldo, S,         \
-                                                                 denom, (int)grid.x, out_img, seq);        \
+      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, true>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,   \
+                   layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, out_img, seq);         \
     else                                                                                                   \
-      attn_warp_kernel<HDV, KVV, REPV, false><<<nb, 128, 0, st>>>(qb, ldq, kf, vf, cstride, layer_off,     \
-                                                                  len, len_add, flags, out, ldo, S,        \
-                                                                  denom, (int)grid.x, nullptr, seq);       \
+      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, false>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,  \
+                   layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, (uint8_t*)nullptr,     \
+                   seq);                                                                                   \
+    (void)e;                                                                                               \
     return true;                                                                                           \
   }
   Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)
@@ -805,6 +971,44 @@ static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st
   Q6W_ROWS(32, 1, 2) Q6W_ROWS(32, 2, 2) Q6W_ROWS(32, 4, 2)
   Q6W_ROWS(32, 1, 4) Q6W_ROWS(32, 2, 4) Q6W_ROWS(32, 4, 4)
 #undef Q6W_ROWS
+  return false;
+}
+
+// The prefill's causal attention (attn_prompt_kernel) when the head layout has
+// an instantiation; returns false to fall back to the per-row kernels.
+static bool launch_attn_prompt(int hd, int KV, int rep, int n_prompts, int max_len, int64_t rows, cudaStream_t st,
+                               const float* qb, int ldq, const void* kc, const void* vc, int64_t cstride,
+                               int64_t layer_off, const int32_t* off, const int32_t* lens, const int32_t* flags,
+                               float denom, float* out, int ldo, uint8_t* out_img, bool kv_half,
+                               bool pdl = false) {
+  cudaError_t e = cudaSuccess;  // a launch error is read by the caller's launch check
+  const float* kf = static_cast<const float*>(kc);
+  const float* vf = static_cast<const float*>(vc);
+  const __half* kh = static_cast<const __half*>(kc);
+  const __half* vh = static_cast<const __half*>(vc);
+#define Q6W_PROMPT(HDV, REPV)                                                                               \
+  if (hd == HDV && rep == REPV) {                                                                           \
+    constexpr int rb = kPromptThreads / REPV;                                                               \
+    const dim3 grid((unsigned)((int64_t)n_prompts * ((max_len + rb - 1) / rb)), (unsigned)KV);              \
+    const dim3 bl(kPromptThreads);                                                                          \
+    if (kv_half && out_img)                                                                                 \
+      e = launch_k(attn_prompt_kernel<HDV, REPV, true, __half>, grid, bl, 0, st, pdl, qb, ldq, kh, vh,      \
+                   cstride, layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo, out_img);      \
+    else if (kv_half)                                                                                       \
+      e = launch_k(attn_prompt_kernel<HDV, REPV, false, __half>, grid, bl, 0, st, pdl, qb, ldq, kh, vh,     \
+                   cstride, layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo,                \
+                   (uint8_t*)nullptr);                                                                      \
+    else if (out_img)                                                                                       \
+      e = launch_k(attn_prompt_kernel<HDV, REPV, true>, grid, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,     \
+                   layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo, out_img);               \
+    else                                                                                                    \
+      e = launch_k(attn_prompt_kernel<HDV, REPV, false>, grid, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,    \
+                   layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo, (uint8_t*)nullptr);     \
+    (void)e;                                                                                                \
+    return true;                                                                                            \
+  }
+  Q6W_PROMPT(16, 1) Q6W_PROMPT(16, 2) Q6W_PROMPT(16, 4) Q6W_PROMPT(32, 1) Q6W_PROMPT(32, 2) Q6W_PROMPT(32, 4)
+#undef Q6W_PROMPT
   return false;
 }
 
@@ -819,6 +1023,8 @@ struct StopSet {
 __global__ void advance_kernel(int n, Work w, const int32_t* __restrict__ prompts, int32_t stride,
                                int32_t new_tokens, StopSet stop, int32_t* sampled,
                                int32_t* n_sampled, int32_t* stop_reason) {
+  grid_dep_launch();
+  grid_dep_wait();
   for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < n; b += gridDim.x * blockDim.x) {
     const unsigned long long key = w.keys[b];
     w.keys[b] = 0ull;
@@ -916,8 +1122,13 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
       e = LinearLauncher<true, EPI_QKV>::run(w.x, dim, n, L.attention_norm, d.norm_eps, ms, q, st);
       if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "qkv linear: %s", cudaGetErrorString(e));
     }
-    if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
-                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq, M->kv_half)) {
+    if (w.poff && launch_attn_prompt(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, w.n_prompts, w.max_len, n, st,
+                                     w.qb, dim, kc, vc, cstride, layer_off, w.poff, w.plens, w.flags, M->denom,
+                                     w.att, dim, nullptr, M->kv_half)) {
+      Q6W_LAUNCH_CHECK("attn_prompt_kernel");
+    } else if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc,
+                                cstride, layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq,
+                                M->kv_half)) {
       Q6W_LAUNCH_CHECK("attn_rows_kernel");
     } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
                                 w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq, M->kv_half)) {
@@ -988,6 +1199,8 @@ static int32_t enqueue_step(const q6w_model* M, int n, const Work& w, float* kc,
 // lanes per sequence, eight values each (dim 128).
 __global__ void embed_tc_kernel(const uint8_t* __restrict__ E, const float* __restrict__ Es, int vocab,
                                 int max_seq, int n, Work w, const float* __restrict__ g, float eps) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int gl = blockIdx.x * blockDim.x + threadIdx.x;
   const int b = gl >> 4, l = gl & 15;
   const bool inb = b < n;
@@ -1028,36 +1241,45 @@ __global__ void embed_tc_kernel(const uint8_t* __restrict__ E, const float* __re
   tc::img_store8(w.xs_img, b, l * 8, 128, u);
 }
 
-static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st) {
+static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st, bool pdl = false) {
   const int items = ((a.n + tc::kM - 1) / tc::kM) * a.n_tiles;
   const int grid = items < sms ? items : sms;
   const size_t smem = tc::smem_bytes();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cudaError_t e;
   if (epi == tc::TEPI_RESNORM && a.pair) {
     // one item per CTA, the two column halves of an M tile in one 2-CTA cluster
-    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)items);
-    cfg.blockDim = dim3(tc::kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_RESNORM>, a);
-    if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tc_gemm_kernel launch: %s", cudaGetErrorString(e));
-    return Q6W_OK;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+    cfg.numAttrs = na;
+    e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_RESNORM>, a);
+  } else {
+    cfg.numAttrs = na;
+    switch (epi) {
+      case tc::TEPI_QKV: e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_QKV>, a); break;
+      case tc::TEPI_RESNORM: e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_RESNORM>, a); break;
+      case tc::TEPI_GLU: e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_GLU>, a); break;
+      case tc::TEPI_STORE: e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_STORE>, a); break;
+      default: e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<tc::TEPI_VOCAB>, a); break;
+    }
   }
-  switch (epi) {
-    case tc::TEPI_QKV: tc::tc_gemm_kernel<tc::TEPI_QKV><<<grid, tc::kThreads, smem, st>>>(a); break;
-    case tc::TEPI_RESNORM: tc::tc_gemm_kernel<tc::TEPI_RESNORM><<<grid, tc::kThreads, smem, st>>>(a); break;
-    case tc::TEPI_GLU: tc::tc_gemm_kernel<tc::TEPI_GLU><<<grid, tc::kThreads, smem, st>>>(a); break;
-    case tc::TEPI_STORE: tc::tc_gemm_kernel<tc::TEPI_STORE><<<grid, tc::kThreads, smem, st>>>(a); break;
-    default: tc::tc_gemm_kernel<tc::TEPI_VOCAB><<<grid, tc::kThreads, smem, st>>>(a); break;
-  }
-  Q6W_LAUNCH_CHECK("tc_gemm_kernel");
+  if (e != cudaSuccess) return fail(Q6W_ERR_CUDA, "tc_gemm_kernel launch: %s", cudaGetErrorString(e));
   return Q6W_OK;
 }
 
@@ -1090,10 +1312,10 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
                                const EpiArgs& vocab_ep, cudaStream_t st, bool with_vocab) {
   const q6w_model_desc& d = M->d;
   const int dim = d.dim, kvr = M->kv_rows, hid = d.hidden_dim, S = d.max_seq_len;
-  embed_tc_kernel<<<(n * 16 + 127) / 128, 128, 0, st>>>(d.tok_embeddings.packed, d.tok_embeddings.scales,
-                                                        d.vocab_size, S, n, w, M->layers[0].attention_norm,
-                                                        d.norm_eps);
-  Q6W_LAUNCH_CHECK("embed_tc_kernel");
+  cudaError_t le = launch_k(embed_tc_kernel, dim3((n * 16 + 127) / 128), dim3(128), 0, st, w.pdl,
+                            d.tok_embeddings.packed, d.tok_embeddings.scales, d.vocab_size, S, n, w,
+                            M->layers[0].attention_norm, d.norm_eps);
+  if (le != cudaSuccess) return fail(Q6W_ERR_CUDA, "embed_tc_kernel launch: %s", cudaGetErrorString(le));
   tc::TcArgs base;
   memset(&base, 0, sizeof(base));
   base.n = n;
@@ -1122,13 +1344,19 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.ep.kc = kc; a.ep.vc = vc; a.ep.cache_stride = cstride; a.ep.layer_off = layer_off;
       a.ep.rope_cos = d.rope_cos; a.ep.rope_sin = d.rope_sin;
       a.ep.hd = M->hd; a.ep.q_rows = dim; a.ep.kv_rows = kvr;
-      if ((rc = tc_launch(tc::TEPI_QKV, a, M->sm_count, st))) return rc;
+      if ((rc = tc_launch(tc::TEPI_QKV, a, M->sm_count, st, w.pdl))) return rc;
     }
-    if (!launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, dim3(n), st, w.qb, dim, kc, vc,
-                          cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img, w.seq,
-                          M->kv_half))
-      return fail(Q6W_ERR_ARG, "no attention kernel for this head layout");
-    Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    if (w.poff && launch_attn_prompt(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, w.n_prompts, w.max_len, n, st,
+                                     w.qb, dim, kc, vc, cstride, layer_off, w.poff, w.plens, w.flags, M->denom,
+                                     nullptr, dim, w.att_img, M->kv_half, w.pdl)) {
+      Q6W_LAUNCH_CHECK("attn_prompt_kernel");
+    } else {
+      if (!launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, dim3(n), st, w.qb, dim, kc, vc,
+                            cstride, layer_off, w.pos, 1, w.flags, nullptr, dim, S, M->denom, w.att_img, w.seq,
+                            M->kv_half, w.pdl))
+        return fail(Q6W_ERR_ARG, "no attention kernel for this head layout");
+      Q6W_LAUNCH_CHECK("attn_rows_kernel");
+    }
     {
       tc::TcArgs a = base;
       a.a_img = w.att_img;
@@ -1137,7 +1365,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.end0 = a.end1 = dim;
       tc_resnorm_tiles(a, n, M->sm_count);
       a.x = w.x; a.gnorm = L.ffn_norm; a.out_img = w.xs_img; a.out_K = dim;
-      if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st))) return rc;
+      if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st, w.pdl))) return rc;
     }
     {
       tc::TcArgs a = base;
@@ -1149,7 +1377,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.N = 128;
       a.n_tiles = hid / 64;
       a.out_img = w.hs_img; a.out_K = hid;
-      if ((rc = tc_launch(tc::TEPI_GLU, a, M->sm_count, st))) return rc;
+      if ((rc = tc_launch(tc::TEPI_GLU, a, M->sm_count, st, w.pdl))) return rc;
     }
     {
       tc::TcArgs a = base;
@@ -1161,7 +1389,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.x = w.x;
       a.gnorm = l + 1 < d.n_layers ? M->layers[l + 1].attention_norm : d.norm;
       a.out_img = w.xs_img; a.out_K = dim;
-      if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st))) return rc;
+      if ((rc = tc_launch(tc::TEPI_RESNORM, a, M->sm_count, st, w.pdl))) return rc;
     }
   }
   if (!with_vocab) return Q6W_OK;
@@ -1179,7 +1407,7 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
   a.ep.gen = w.gen;
   a.ep.plen = w.plen;
   a.ep.vocab = d.vocab_size;
-  return tc_launch(tc::TEPI_VOCAB, a, M->sm_count, st);
+  return tc_launch(tc::TEPI_VOCAB, a, M->sm_count, st, w.pdl);
 }
 
 // ---- batched prefill: rows are prompt tokens --------------------------------
@@ -1553,8 +1781,13 @@ static int32_t enqueue_step_tcg(const q6w_model* M, int n, const Work& w, float*
       a.ep.hd = M->hd; a.ep.q_rows = dim; a.ep.kv_rows = kvr;
       if ((rc = tcg_launch(tcg::GEPI_QKV, a, M->sm_count, st))) return rc;
     }
-    if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc, cstride,
-                         layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq, M->kv_half)) {
+    if (w.poff && launch_attn_prompt(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, w.n_prompts, w.max_len, n, st,
+                                     w.qb, dim, kc, vc, cstride, layer_off, w.poff, w.plens, w.flags, M->denom,
+                                     w.att, dim, nullptr, M->kv_half)) {
+      Q6W_LAUNCH_CHECK("attn_prompt_kernel");
+    } else if (launch_attn_rows(M->hd, d.n_kv_heads, d.n_heads / d.n_kv_heads, agrid, st, w.qb, dim, kc, vc,
+                                cstride, layer_off, w.pos, 1, w.flags, w.att, dim, S, M->denom, nullptr, w.seq,
+                                M->kv_half)) {
       Q6W_LAUNCH_CHECK("attn_rows_kernel");
     } else if (launch_attn_head(M->hd, n, d.n_heads, d.n_kv_heads, st, w.qb, dim, kc, vc, cstride, layer_off,
                                 w.pos, 1, w.flags, w.att, dim, S, M->denom, w.seq, M->kv_half)) {
@@ -1899,6 +2132,10 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
     const char* onp = getenv("Q6W_PDEC");
     M->use_pdec = (onp && onp[0] == '1') && major == 10 && (pdec_shapes_ok(M) || pdec_off("shapes")) &&
                   pdec_setup(M);
+    // Programmatic dependent launch across the tensor-core step measured slower on the 8192-sequence
+    // decode (116.5 against 112.1 ms a generation), as it did across the general tensor-core step.
+    const char* pdl = getenv("Q6W_PDL");
+    M->use_pdl = pdl && pdl[0] == '1';
   }
   *out = M;
   return Q6W_OK;
@@ -2074,7 +2311,9 @@ static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& 
     v.y = w.logits;  // the raw logits row of every sequence, for the sampler
     v.ldy = M->d.vocab_size;
   }
-  int32_t st = enqueue_step(M, a->n_seqs, w, a->k_cache, a->v_cache, a->cache_seq_stride, v,
+  Work wp = w;
+  wp.pdl = M->use_pdl;
+  int32_t st = enqueue_step(M, a->n_seqs, wp, a->k_cache, a->v_cache, a->cache_seq_stride, v,
                             M->cap_stream);
   if (st == Q6W_OK && sp) {
     smp::Args sa;
@@ -2091,14 +2330,15 @@ static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& 
     sa.pos = w.pos;
     sa.plen = w.plen;
     sa.p = *sp;
-    smp::sample_kernel<<<a->n_seqs, smp::kThreads, smp::smem_bytes(M->d.vocab_size), M->cap_stream>>>(sa);
-    if (cudaGetLastError() != cudaSuccess) st = fail(Q6W_ERR_CUDA, "sample_kernel launch failed");
+    if (launch_k(smp::sample_kernel, dim3(a->n_seqs), dim3(smp::kThreads), smp::smem_bytes(M->d.vocab_size),
+                 M->cap_stream, wp.pdl, sa) != cudaSuccess)
+      st = fail(Q6W_ERR_CUDA, "sample_kernel launch failed");
   }
   if (st == Q6W_OK) {
-    advance_kernel<<<grid_for(a->n_seqs, 256), 256, 0, M->cap_stream>>>(
-        a->n_seqs, w, a->prompts, a->prompt_stride, a->new_tokens, stop, a->sampled, a->n_sampled,
-        a->stop_reason);
-    if (cudaGetLastError() != cudaSuccess) st = fail(Q6W_ERR_CUDA, "advance_kernel launch failed");
+    if (launch_k(advance_kernel, dim3(grid_for(a->n_seqs, 256)), dim3(256), 0, M->cap_stream, wp.pdl, a->n_seqs, w,
+                 a->prompts, a->prompt_stride, a->new_tokens, stop, a->sampled, a->n_sampled,
+                 a->stop_reason) != cudaSuccess)
+      st = fail(Q6W_ERR_CUDA, "advance_kernel launch failed");
   }
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamEndCapture(M->cap_stream, &graph);
@@ -2178,6 +2418,11 @@ extern "C" int32_t q6w_prefill(const q6w_model* M, int32_t n_prompts, const int3
       n_prompts, rows, prompts, prompt_stride, prompt_lens, max_prompt_len, M->d.vocab_size, off, w, seq);
   Q6W_LAUNCH_CHECK("prefill_rows_kernel");
   w.seq = seq;
+  w.poff = off;
+  w.plens = prompt_lens;
+  w.n_prompts = n_prompts;
+  w.max_len = max_prompt_len;
+  w.pdl = M->use_pdl;
   EpiArgs none;
   memset(&none, 0, sizeof(none));
   if ((st = enqueue_step(M, rows, w, k_cache, v_cache, cache_seq_stride, none, s, false))) return st;
@@ -2243,6 +2488,11 @@ extern "C" int32_t q6w_forward_all(const q6w_model* M, int32_t n_prompts, const 
       n_prompts, rows, prompts, prompt_stride, prompt_lens, max_prompt_len, M->d.vocab_size, off, w, seq);
   Q6W_LAUNCH_CHECK("prefill_rows_kernel");
   w.seq = seq;
+  w.poff = off;
+  w.plens = prompt_lens;
+  w.n_prompts = n_prompts;
+  w.max_len = max_prompt_len;
+  w.pdl = M->use_pdl;
   // every row through the layers and the vocab head (final RMSNorm + tied embedding): the logits of
   // every position, row off[i] + j for position j of prompt i
   EpiArgs v;

@@ -331,6 +331,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(Args a) {
   __shared__ int redi[32];
   __shared__ unsigned long long redk[32];
   __shared__ float s_coin;
+  grid_dep_launch();
+  grid_dep_wait();
   const int b = blockIdx.x;
   if (a.flags) {
     const int f = a.flags[b];

@@ -258,15 +258,20 @@ __device__ __forceinline__ int b_segments(const TcArgs& a, int epi, int nt, Seg 
 
 // Thread 0: start the bulk copies of stage `ks` of item (mt, nt): the A
 // stage when `want_a`, the packed B rows (all K) and their scales when
-// `want_b`; all complete on `bar`.
+// `want_b`; all complete on `bar`.  With `arrive` false the copies only add
+// their bytes to the barrier's count (a later call arrives).
 __device__ __forceinline__ void issue_loads(const TcArgs& a, int epi, int mt, int nt, int ks, bool want_a,
-                                            bool want_b, uint8_t* sA, uint8_t* stage, uint64_t* bar) {
+                                            bool want_b, uint8_t* sA, uint8_t* stage, uint64_t* bar,
+                                            bool arrive = true) {
   const uint32_t rb = (uint32_t)a.K * 3 / 4;
   Seg sg[3];
   const int nseg = b_segments(a, epi, nt, sg);
   uint32_t bytes = want_a ? 3 * 32768 : 0;
   if (want_b) bytes += (uint32_t)a.N * (rb + 4);
-  mbar_expect_tx(bar, bytes);
+  if (arrive)
+    mbar_expect_tx(bar, bytes);
+  else
+    mbar_expect_tx_only(bar, bytes);
   if (want_a) {
     const uint8_t* src = a.a_img + (int64_t)mt * 3 * a.K * 256 + (int64_t)ks * 32768;
 #pragma unroll
@@ -326,7 +331,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
   const int kstages = a.K / kKC;
   const uint32_t rb = (uint32_t)a.K * 3 / 4;
   uint32_t ph_mma = 0, ph_ld = 0;
-  if (tid == 0 && it0 < it1) issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 0, true, true, sA, stage, &ld_bar);
+  // The weights do not depend on the preceding grid: their copies start
+  // before the programmatic-dependency wait, the activation tile after it.
+  grid_dep_launch();
+  if (tid == 0 && it0 < it1)
+    issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 0, false, true, sA, stage, &ld_bar, false);
+  grid_dep_wait();
+  if (tid == 0 && it0 < it1) issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 0, true, false, sA, stage, &ld_bar);
 
   for (int it = it0; it < it1 && !timed_out; ++it) {
     const int mt = it / a.n_tiles, nt = it % a.n_tiles;
