@@ -1247,7 +1247,7 @@ static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st,
   const size_t smem = tc::smem_bytes();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(tc::kThreads);
+  cfg.blockDim = dim3(tc::threads_for(epi));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];

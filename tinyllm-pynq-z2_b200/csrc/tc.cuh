@@ -167,6 +167,19 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // 32 consecutive FP32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -187,6 +200,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // ---- GEMM --------------------------------------------------------------------
 
 enum { TEPI_QKV = 0, TEPI_RESNORM = 1, TEPI_GLU = 2, TEPI_VOCAB = 3, TEPI_STORE = 4 };
+
+// Threads per CTA.  The weight expansion and the SwiGLU / argmax epilogues
+// are latency-bound at one CTA per SM, so those kernels run 16 warps (each
+// TMEM lane quadrant read by four warps, a quarter of the columns each); the
+// QKV and residual + RMSNorm epilogues hold whole row blocks in registers
+// and keep 8 warps.
+__host__ __device__ constexpr int threads_for(int epi) {
+  return (epi == TEPI_GLU || epi == TEPI_VOCAB) ? 512 : kThreads;
+}
 
 // Rows per N tile of the plain linear (TEPI_STORE) on this kernel, or 0 when
 // the shape does not fit it: K a multiple of 128, N in {256, 128, 64}
@@ -292,7 +314,9 @@ __device__ __forceinline__ void issue_loads(const TcArgs& a, int epi, int mt, in
 // Shared memory: [A stage 96 KB][B tile N x 128 bf16, 64 KB][packed B rows + scales, <= 37 KB]
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
+__global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) {
+  constexpr int NT = threads_for(EPI);
+  constexpr int kParts = NT / 128;  // warps reading each TMEM lane quadrant (column parts)
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t mma_bar, ld_bar;
   __shared__ uint32_t tmem_base;
@@ -351,9 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
       if (timed_out) break;
       // expand N rows x 128 codes (columns 128ks..) from the staged bytes to bf16
       if (ks == 0)
-        for (int j = tid; j < a.N; j += kThreads)
+        for (int j = tid; j < a.N; j += NT)
           sscale[j] = reinterpret_cast<const float*>(stage + (size_t)a.N * rb)[j];
-      for (int i = tid; i < a.N * 8; i += kThreads) {
+      for (int i = tid; i < a.N * 8; i += NT) {
         const int j = i >> 3, u = i & 7;
         const uint32_t* pw = reinterpret_cast<const uint32_t*>(stage + j * rb + (ks * 8 + u) * 12);
         const uint32_t w0 = pw[0], w1 = pw[1], w2 = pw[2];
@@ -410,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
     // ---- epilogue: lane quadrant q = warp & 3 holds sequence rows 32q..32q+31
     // (TMEM lanes); warps q and q + 4 take the two halves of the columns.
     const int row = ((warp & 3) << 5) | (tid & 31);
-    const int half = warp >> 2;
+    const int half = warp >> 2;  // the column part (halves at 8 warps, quarters at 16)
     const int64_t m = (int64_t)mt * kM + row;
     const bool live = m < a.n;
     const uint32_t lane_addr = taddr + ((uint32_t)((warp & 3) * 32) << 16);
@@ -421,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
                         ep.pos[m] >= ep.plen[m] - 1;
       float bv = -INFINITY;
       int bi = -1;
-      const int cb = half * (a.N >> 1), ce = cb + (a.N >> 1);
+      const int cb = half * (a.N / kParts), ce = cb + a.N / kParts;
       for (int c0 = cb; c0 < ce; c0 += 32) {
         float v[32];
         tmem_ld32(lane_addr + c0, v);
@@ -667,17 +691,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcArgs a) {
           img_store8(a.out_img, mr, col, 128, u8);
         }
       }
-    } else if (EPI == TEPI_GLU) {  // columns j (W1) and H + j (W3), H = N/2; this thread: j in (H/2)*half..
-      const int H = a.N >> 1, hq = H >> 1;
+    } else if (EPI == TEPI_GLU) {  // columns j (W1) and H + j (W3), H = N/2; this thread: j in (H/kParts)*part..
+      const int H = a.N >> 1, hq = H / kParts;
 #pragma unroll 1
-      for (int cc = 0; cc < hq; cc += 32) {
+      for (int cc = 0; cc < hq; cc += 16) {
         const int c0 = half * hq + cc;
-        float va[32], vb[32];
-        tmem_ld32(lane_addr + c0, va);
-        tmem_ld32(lane_addr + H + c0, vb);
+        float va[16], vb[16];
+        tmem_ld16(lane_addr + c0, va);
+        tmem_ld16(lane_addr + H + c0, vb);
         if (!live) continue;
 #pragma unroll
-        for (int k0 = 0; k0 < 32; k0 += 8) {
+        for (int k0 = 0; k0 < 16; k0 += 8) {
           float h8[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i)
