@@ -167,6 +167,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // 32 consecutive FP32 columns of this thread's TMEM lane.
+// Split cluster barrier: arrive (release) now, wait (acquire) later.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
@@ -365,6 +369,49 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
 
   for (int it = it0; it < it1 && !timed_out; ++it) {
     const int mt = it / a.n_tiles, nt = it % a.n_tiles;
+    // Epilogue inputs that do not depend on the MMA are loaded first, so they
+    // are in flight during the tile loads, the expansion and the MMAs.
+    // QKV: this thread's row state and the RoPE rotation of the 16 pairs of a
+    // 32-column chunk (chunks start on a head boundary: columns are multiples
+    // of 32 and head_dim is 16 or 32, so pair p turns by frequency p mod hd/2).
+    bool q_ok = false;
+    int q_pos = 0;
+    int64_t q_crow = 0;
+    float cp[16], sp[16];
+    if (EPI == TEPI_QKV) {
+      const EpiArgs& ep = a.ep;
+      const int64_t me = (int64_t)mt * kM + (((warp & 3) << 5) | (tid & 31));
+      q_ok = me < a.n && !(ep.flags[me] & SEQ_INVALID);
+      q_pos = q_ok ? ep.pos[me] : 0;
+      q_crow = q_ok && ep.seq ? ep.seq[me] : me;
+      const int hh = ep.hd >> 1;  // 8 or 16 rotation frequencies
+#pragma unroll
+      for (int p = 0; p < 16; ++p) {
+        cp[p] = q_ok ? __ldg(ep.rope_cos + (int64_t)q_pos * hh + (p & (hh - 1))) : 0.0f;
+        sp[p] = q_ok ? __ldg(ep.rope_sin + (int64_t)q_pos * hh + (p & (hh - 1))) : 0.0f;
+      }
+    }
+    // RESNORM: the residual rows of this thread's passes and its norm weights.
+    constexpr int kPass = kM / 16;  // at most 8 passes of 2 rows per warp (4 rows in pair mode)
+    float4 ox[kPass][2];
+    float gw[8];
+    if (EPI == TEPI_RESNORM) {
+      const int lane = tid & 31;
+      const int lpr = a.N >> 3, rpi = 32 / lpr;
+      const int sub = lane / lpr, cb = 8 * (lane % lpr);
+      const int col = nt * a.N + cb;
+      const int npass = (kM / 8) / rpi;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gw[i] = __ldg(a.gnorm + col + i);
+#pragma unroll
+      for (int i = 0; i < kPass; ++i) {
+        const int64_t mr = (int64_t)mt * kM + 16 * warp + rpi * i + sub;
+        const float4* xr = reinterpret_cast<const float4*>(a.x + mr * 128 + col);
+        const bool in = i < npass && mr < a.n;
+        ox[i][0] = in ? xr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ox[i][1] = in ? xr[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
     for (int ks = 0; ks < kstages; ++ks) {
       if (!mbar_wait(&ld_bar, ph_ld)) {
         if (tid == 0) atomicOr(a.err, kErrTimeout);
@@ -513,20 +560,10 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       // scale and RoPE, into sB unit c4 of row r at r*32 + (c4 ^ (r & 7));
       // E2: lanes of a row store contiguous runs of q, k and v.
       const EpiArgs& ep = a.ep;
-      const bool ok = live && !(ep.flags[m] & SEQ_INVALID);
-      const int pos = ok ? ep.pos[m] : 0;
+      const bool ok = q_ok;
       s_ok[row] = ok;
-      s_pos[row] = pos;
-      s_crow[row] = ok && ep.seq ? ep.seq[m] : m;
-      const int hh = ep.hd >> 1;  // 8 or 16 rotation frequencies
-      float cs[16], sn[16];
-      if (ok) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          cs[i] = i < hh ? __ldg(ep.rope_cos + (int64_t)pos * hh + i) : 0.0f;
-          sn[i] = i < hh ? __ldg(ep.rope_sin + (int64_t)pos * hh + i) : 0.0f;
-        }
-      }
+      s_pos[row] = q_pos;
+      s_crow[row] = q_crow;
       float4* st4 = reinterpret_cast<float4*>(sB);
       const int lane = tid & 31;
 #pragma unroll 1
@@ -552,11 +589,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
           if (ok && v0 < ep.q_rows + ep.kv_rows) {
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
-              const int j = ((v0 + i) & (ep.hd - 1)) >> 1;
-              float c = cs[0], sv = sn[0];
-#pragma unroll
-              for (int f = 1; f < 16; ++f)
-                if (f == j) { c = cs[f]; sv = sn[f]; }
+              const float c = cp[i >> 1], sv = sp[i >> 1];
               const float ra = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + 1], sv));
               const float rb = __fadd_rn(__fmul_rn(v[i], sv), __fmul_rn(v[i + 1], c));
               v[i] = ra;
@@ -618,21 +651,8 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       const int lpr = a.N >> 3, rpi = 32 / lpr;  // lanes per row, rows per warp pass
       const int sub = lane / lpr, cl8 = lane % lpr, cb = 8 * cl8;
       const int col = nt * a.N + cb;  // column of x and of the image
-      float gw[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) gw[i] = __ldg(a.gnorm + col + i);
-      constexpr int kPass = kM / 16;  // at most 8 passes of 2 rows per warp (4 rows in pair mode)
       const int npass = (kM / 8) / rpi;
-      // the residual rows of all passes are loaded first, so the loads overlap
-      float4 ox[kPass][2];
-#pragma unroll
-      for (int i = 0; i < kPass; ++i) {
-        const int64_t mr = (int64_t)mt * kM + 16 * warp + rpi * i + sub;
-        const float4* xr = reinterpret_cast<const float4*>(a.x + mr * 128 + col);
-        const bool in = i < npass && mr < a.n;
-        ox[i][0] = in ? xr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
-        ox[i][1] = in ? xr[1] : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      // ox (the residual rows of all passes) and gw were loaded at the item's start
       float xk[kPass][8];
       float ssk[kPass];
 #pragma unroll
@@ -665,8 +685,8 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       }
       if (a.pair) {
         // both halves of every row: the partial sums meet through distributed
-        // shared memory; the second barrier keeps this CTA's array alive
-        // until the peer has read it
+        // shared memory; the second barrier (arrive here, wait before the CTA
+        // exits) keeps this CTA's array alive until the peer has read it
         cg::cluster_group cl = cg::this_cluster();
         cl.sync();
         const float* peer = cl.map_shared_rank(s_ssp, nt ^ 1);
@@ -677,7 +697,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
             ssk[i] = nt == 0 ? __fadd_rn(ssk[i], peer[r]) : __fadd_rn(peer[r], ssk[i]);
           }
         }
-        cl.sync();
+        cluster_arrive();
         pair_synced = 2;
       }
 #pragma unroll
@@ -714,9 +734,14 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
     __syncthreads();
   }
   // a pair CTA that stopped early still takes its two cluster barriers, so
-  // the peer's waits end
-  if (EPI == TEPI_RESNORM && a.pair)
-    for (; pair_synced < 2; ++pair_synced) cg::this_cluster().sync();
+  // the peer's waits end; the second one's wait comes last
+  if (EPI == TEPI_RESNORM && a.pair) {
+    if (pair_synced < 2) {
+      cg::this_cluster().sync();
+      cluster_arrive();
+    }
+    cluster_wait();
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
