@@ -939,7 +939,7 @@ static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st
                              const int32_t* len, int len_add, const int32_t* flags, float* out, int ldo,
                              int S, float denom, uint8_t* out_img = nullptr, const int32_t* seq = nullptr,
                              bool kv_half = false, bool pdl = false) {
-  cudaError_t e = cudaSuccess;  // a launch error is read by the caller's launch check
+  // a launch error is left for the caller's launch check (cudaGetLastError)
   const float* kf = static_cast<const float*>(kc);
   const float* vf = static_cast<const float*>(vc);
   const __half* kh = static_cast<const __half*>(kc);
@@ -948,20 +948,19 @@ static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st
   if (hd == HDV && KV == KVV && rep == REPV) {                                                             \
     const dim3 nb(((int)grid.x + 3) / 4), bl(128);                                                         \
     if (kv_half && out_img)                                                                                \
-      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, true, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,    \
+      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, true, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,    \
                    cstride, layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, out_img, seq); \
     else if (kv_half)                                                                                      \
-      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, false, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,   \
+      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, false, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,   \
                    cstride, layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x,               \
                    (uint8_t*)nullptr, seq);                                                                \
     else if (out_img)                                                                                      \
-      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, true>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,   \
+      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, true>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,   \
                    layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, out_img, seq);         \
     else                                                                                                   \
-      e = launch_k(attn_warp_kernel<HDV, KVV, REPV, false>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,  \
+      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, false>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,  \
                    layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, (uint8_t*)nullptr,     \
                    seq);                                                                                   \
-    (void)e;                                                                                               \
     return true;                                                                                           \
   }
   Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)
@@ -981,7 +980,7 @@ static bool launch_attn_prompt(int hd, int KV, int rep, int n_prompts, int max_l
                                int64_t layer_off, const int32_t* off, const int32_t* lens, const int32_t* flags,
                                float denom, float* out, int ldo, uint8_t* out_img, bool kv_half,
                                bool pdl = false) {
-  cudaError_t e = cudaSuccess;  // a launch error is read by the caller's launch check
+  // a launch error is left for the caller's launch check (cudaGetLastError)
   const float* kf = static_cast<const float*>(kc);
   const float* vf = static_cast<const float*>(vc);
   const __half* kh = static_cast<const __half*>(kc);
@@ -992,19 +991,18 @@ static bool launch_attn_prompt(int hd, int KV, int rep, int n_prompts, int max_l
     const dim3 grid((unsigned)((int64_t)n_prompts * ((max_len + rb - 1) / rb)), (unsigned)KV);              \
     const dim3 bl(kPromptThreads);                                                                          \
     if (kv_half && out_img)                                                                                 \
-      e = launch_k(attn_prompt_kernel<HDV, REPV, true, __half>, grid, bl, 0, st, pdl, qb, ldq, kh, vh,      \
+      (void)launch_k(attn_prompt_kernel<HDV, REPV, true, __half>, grid, bl, 0, st, pdl, qb, ldq, kh, vh,      \
                    cstride, layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo, out_img);      \
     else if (kv_half)                                                                                       \
-      e = launch_k(attn_prompt_kernel<HDV, REPV, false, __half>, grid, bl, 0, st, pdl, qb, ldq, kh, vh,     \
+      (void)launch_k(attn_prompt_kernel<HDV, REPV, false, __half>, grid, bl, 0, st, pdl, qb, ldq, kh, vh,     \
                    cstride, layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo,                \
                    (uint8_t*)nullptr);                                                                      \
     else if (out_img)                                                                                       \
-      e = launch_k(attn_prompt_kernel<HDV, REPV, true>, grid, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,     \
+      (void)launch_k(attn_prompt_kernel<HDV, REPV, true>, grid, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,     \
                    layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo, out_img);               \
     else                                                                                                    \
-      e = launch_k(attn_prompt_kernel<HDV, REPV, false>, grid, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,    \
+      (void)launch_k(attn_prompt_kernel<HDV, REPV, false>, grid, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,    \
                    layer_off, off, lens, max_len, KV, rows, flags, denom, out, ldo, (uint8_t*)nullptr);     \
-    (void)e;                                                                                                \
     return true;                                                                                            \
   }
   Q6W_PROMPT(16, 1) Q6W_PROMPT(16, 2) Q6W_PROMPT(16, 4) Q6W_PROMPT(32, 1) Q6W_PROMPT(32, 2) Q6W_PROMPT(32, 4)
