@@ -16,13 +16,16 @@ There is no CPU path: constructing the model without a CUDA device or
 without the compiled library raises.
 """
 
+import tempfile
 import time
+from pathlib import Path
 from types import SimpleNamespace
 
 import numpy as np
 import torch
 
 from . import _lib
+from . import format as fmt
 from .format import Q6WImage, ffn_dim
 from .ops import DeviceImage
 
@@ -72,24 +75,34 @@ class Q6WCudaTransformer:
             device = torch.device("cuda", torch.cuda.current_device())
         self._lib = _lib.load()
         self.device = device
+        if kv_dtype not in (torch.float32, torch.float16):
+            raise ValueError("kv_dtype must be torch.float32 or torch.float16")
+        self._max_seq_len = max_seq_len
+        self._ws = {}
+        self._attach(image, kv_dtype)
+
+    def _attach(self, image, kv_dtype):
+        """Upload ``image`` and create the device model (replacing any earlier one)."""
+        old = getattr(self, "_handle", None)
         self.image = image
-        self.args = runtime_args(image.model_args, max_seq_len)
+        self.args = runtime_args(image.model_args, self._max_seq_len)
         a = self.args
         self.n_kv_heads = a.n_kv_heads or a.n_heads
         self.head_dim = a.dim // a.n_heads
         self.hidden_dim = ffn_dim(vars(a))
-        with torch.cuda.device(device):
-            self.dimg = DeviceImage(image, device)
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            if old is not None and old.value:
+                self._lib.q6w_model_destroy(old)
+                self._handle = None
+            self.dimg = DeviceImage(image, self.device)
             cos, sin = rope_tables(self.head_dim, a.max_seq_len)
-            self.freqs_cos = cos.to(device)
-            self.freqs_sin = sin.to(device)
+            self.freqs_cos = cos.to(self.device)
+            self.freqs_sin = sin.to(self.device)
             self._build_desc()
             handle = ctypes_void()
             _lib.check(self._lib.q6w_model_create(self._desc, handle), "q6w_model_create")
             self._handle = handle
-            self._ws = {}
-        if kv_dtype not in (torch.float32, torch.float16):
-            raise ValueError("kv_dtype must be torch.float32 or torch.float16")
         _lib.check(self._lib.q6w_model_set_kv_dtype(self._handle, 1 if kv_dtype == torch.float16 else 0),
                    "q6w_model_set_kv_dtype")
         self.kv_dtype = kv_dtype
@@ -138,6 +151,40 @@ class Q6WCudaTransformer:
     # -- nn.Module-style no-ops kept for drop-in use ----------------------------
     def eval(self):
         return self
+
+    def load_state_dict(self, state_dict, strict=True):
+        """Take FP32 weights by name, as ``CachedTransformer.load_state_dict``
+        does (evaluate_q6w.py:158-163): every quantized tensor is quantized and
+        packed on this GPU with the reference's row rule (q6w_format.py:84-98),
+        so the model equals what ``export_q6w`` + ``from_q6w`` give for the same
+        weights; norm weights are used as given.  A state that holds a Q6W
+        file's dequantized weights round-trips to the same codes, with scales
+        within one rounding of the file's.
+
+        The model needs every quantized and norm tensor, so missing keys raise
+        whatever ``strict`` says; with ``strict``, keys the model does not have
+        raise too (``output.weight``, tied to the embedding, is accepted when
+        it equals ``tok_embeddings.weight``).  Returns (missing, unexpected)
+        key lists, as torch does."""
+        args = dict(self.image.model_args)
+        n_layers = int(args["n_layers"])
+        want = fmt.quant_keys(n_layers) + fmt.norm_keys(n_layers)
+        missing = [k for k in want if k not in state_dict]
+        unexpected = [k for k in state_dict if k not in want and k != "output.weight"]
+        if "output.weight" in state_dict and "tok_embeddings.weight" in state_dict and not torch.equal(
+                state_dict["output.weight"].detach().cpu(), state_dict["tok_embeddings.weight"].detach().cpu()):
+            raise ValueError("output.weight must equal tok_embeddings.weight (the head is tied)")
+        if missing:
+            raise RuntimeError(f"state_dict lacks tensors the model needs: {missing[:4]}")
+        if strict and unexpected:
+            raise RuntimeError(f"unexpected keys in state_dict: {unexpected[:4]}")
+        state = {k: state_dict[k].detach().float().contiguous() for k in want}
+        with tempfile.TemporaryDirectory() as d:
+            b, m = Path(d) / "state.bin", Path(d) / "state.json"
+            fmt.write_q6w(state, args, b, m, {"load_state_dict": True}, device=self.device)
+            image = Q6WImage(b, m)
+        self._attach(image, self.kv_dtype)
+        return SimpleNamespace(missing_keys=[], unexpected_keys=unexpected)
 
     def to(self, device):
         if torch.device(device) != self.device and not (torch.device(device).type == "cuda" and torch.device(device).index is None):
@@ -426,6 +473,15 @@ class Q6WCudaTransformer:
                                  stop_token_bias if stop_ids else 0.0, bias_after,
                                  torch.tensor(signed, dtype=torch.int64, device=self.device))
         return self.generate_greedy(prompts, new_tokens, stop_ids, min_new_tokens, keep_logits, sampling=sampling)
+
+    def decode_greedy_batch(self, prompts, new_tokens, stop_ids=None, min_new_tokens=0):
+        """Batched greedy decode of a list of prompt id lists: (ids,
+        per_step_argmax).  ids[b] is what ``torch_benchmark.generate`` returns
+        for request b at temperature 0 (at most ``new_tokens`` ids, a stop id
+        not appended); per_step_argmax[b] is the argmax of every decode step
+        (the stop id, when one ended the request, last)."""
+        r = self.generate_greedy(prompts, new_tokens, tuple(stop_ids or ()), min_new_tokens)
+        return r.generated, r.sampled
 
     def generate_greedy(self, prompts, new_tokens, stop_ids=(), min_new_tokens=0, keep_logits=False, sampling=None):
         """Greedy generation for a list of prompt id lists; host results.
