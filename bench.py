@@ -60,7 +60,8 @@ def parse():
     ap.add_argument("--profile-gemv", metavar="ROWSxCOLS", default=None,
                     help="only run one B=1 Q6W GEMV of that shape 4 times (a small case for ncu) and exit")
     ap.add_argument("--sweep-only", action="store_true", help="only run the isolated linear sweep and print it")
-    ap.add_argument("--profile", choices=("b1", "prefill", "prefill_full", "sampler", "linear", "quantize"), default=None,
+    ap.add_argument("--profile", choices=("b1", "prefill", "prefill_full", "attn", "sampler", "linear", "quantize"),
+                    default=None,
                     help="only run one small case of that path a few times (for an ncu capture) and exit")
     ap.add_argument("--profile-scaled-step", type=int, nargs="?", const=1, default=None, metavar="N",
                     help="only run N short requests (2 + 3 tokens, default N=1) of the 1.1B-shape config and exit")
@@ -941,6 +942,7 @@ def profile_case(name):
     b1 -- a B=1 request of the tiny model (20 + 128 tokens, the cluster kernel);
     prefill -- 256 of the 2048 ragged prompts in one q6w_prefill;
     prefill_full -- all 2048 ragged prompts (lengths U[8, 256]) in one q6w_prefill;
+    attn -- decode attention alone, 8192 sequences (tiny heads) at lengths 20 and 147;
     sampler -- the sampler op on 8192 rows of 4096 logits (top-p 0.9, T 0.8);
     linear -- the 4096 x 128 linear at N = 4096 on the tensor cores;
     quantize -- the device writer on a 5632 x 2048 matrix."""
@@ -974,6 +976,17 @@ def profile_case(name):
         pr, ln = torch.from_numpy(ids).to(dev), torch.from_numpy(lens).to(dev)
         caches = model.new_batch_cache(2048)
         run = lambda: model.prefill_batch_device(pr, ln, 256, int(lens.sum()), caches=caches)
+    elif name == "attn":
+        # decode attention alone (the public op, non-split output), 8192 sequences at lengths 20 and 147
+        k = torch.randn(8192, 160, 4, 16, device=dev)
+        v = torch.randn(8192, 160, 4, 16, device=dev)
+        q = torch.randn(8192, 8, 16, device=dev)
+        l20 = torch.full((8192,), 20, dtype=torch.int32, device=dev)
+        l147 = torch.full((8192,), 147, dtype=torch.int32, device=dev)
+
+        def run():
+            ops.gqa_attention(q, k, v, l20, 2)
+            ops.gqa_attention(q, k, v, l147, 2)
     elif name == "sampler":
         g = torch.Generator().manual_seed(1)
         logits = (torch.randn(8192, 4096, generator=g) * 2).to(dev)

@@ -76,3 +76,4 @@ def test_pdl_step_bit_identical(tiny_files, tiny):
         P = len(p) + len(a.sampled[i]) - 1  # positions the generation wrote
         assert torch.equal(a.caches[0][i, :, :P], b.caches[0][i, :, :P]), i
         assert torch.equal(a.caches[1][i, :, :P], b.caches[1][i, :, :P]), i
+

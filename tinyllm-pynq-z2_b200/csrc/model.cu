@@ -656,44 +656,21 @@ static bool attn_rows_instantiated(int hd, int KV, int rep) {
 // 16 dims per lane), prefetching the next pass's rows while it computes the
 // current one, with an online softmax per lane for the REP query heads of
 // its kv head; lanes holding the same (kv head, dims) merge by shuffles.
-template <int HD, int KV, int REP, bool SPLIT, typename KT = float>
-__global__ void __launch_bounds__(128) attn_warp_kernel(
-    const float* __restrict__ qb, int ldq, const KT* __restrict__ kc, const KT* __restrict__ vc,
-    int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
-    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom, int n,
-    uint8_t* __restrict__ out_img, const int32_t* __restrict__ seq) {
+// One sequence's attention from its query rows (q) and the K/V rows of the
+// first pass (kn, vn: row t_lane); kb / vb are this lane's cache columns at
+// row 0.  Shared by the per-sequence and the streaming kernels, so both give
+// the same bits.
+template <int HD, int KV, int REP, bool SPLIT, typename KT>
+__device__ __forceinline__ void attn_rows_body(const float (&q)[REP][16], float4 (&kn)[4], float4 (&vn)[4],
+                                               const KT* __restrict__ kb, const KT* __restrict__ vb, int T, int b,
+                                               int lane, float denom, float* __restrict__ out, int ldo,
+                                               uint8_t* __restrict__ out_img) {
   constexpr int C = HD / 16;
   constexpr int R = KV * C;
   constexpr int PPW = 32 / R;
-  constexpr int ROW = KV * HD;  // floats per cached row
-  static_assert(32 % R == 0, "a row must map onto a power-of-two lane group");
-  grid_dep_launch();
-  grid_dep_wait();
-  const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (b >= n) return;
+  constexpr int ROW = KV * HD;
   const int r = lane % R, kvh = r / C, chunk = r % C;
-  int T = len[b] + len_add;
-  T = T > S ? S : T;
-  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
-    if (SPLIT) {
-      const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int k = lane * 8; k < KV * REP * HD; k += 256) tc::img_store8(out_img, b, k, KV * REP * HD, z);
-    } else {
-      for (int i = lane; i < KV * REP * HD; i += 32) out[(int64_t)b * ldo + i] = 0.0f;
-    }
-    return;
-  }
-  float q[REP][16];
-#pragma unroll
-  for (int j = 0; j < REP; ++j) {
-    const float4* qp = reinterpret_cast<const float4*>(qb + (int64_t)b * ldq + (kvh * REP + j) * HD + chunk * 16);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = qp[i];
-      q[j][4 * i] = v.x; q[j][4 * i + 1] = v.y; q[j][4 * i + 2] = v.z; q[j][4 * i + 3] = v.w;
-    }
-  }
+  const int t_lane = lane / R;
   float m[REP], l[REP], acc[REP][16];
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
@@ -701,18 +678,6 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
     l[j] = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[j][i] = 0.0f;
-  }
-  const int64_t crow = seq ? seq[b] : b;
-  const KT* kb = kc + crow * cstride + layer_off + r * 16;
-  const KT* vb = vc + crow * cstride + layer_off + r * 16;
-  const int t_lane = lane / R;
-  float4 kn[4], vn[4];
-  if (t_lane < T) {
-    load_kv16(kb + (int64_t)t_lane * ROW, kn);
-    load_kv16(vb + (int64_t)t_lane * ROW, vn);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) kn[i] = vn[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int t0 = 0; t0 < T; t0 += PPW) {
     const int t = t0 + t_lane;
@@ -791,6 +756,66 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
       }
     }
   }
+}
+
+// Zeros for a sequence with nothing to attend (invalid, or no positions).
+template <int HD, int KV, int REP, bool SPLIT>
+__device__ __forceinline__ void attn_rows_zero(int b, int lane, float* __restrict__ out, int ldo,
+                                               uint8_t* __restrict__ out_img) {
+  if (SPLIT) {
+    const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = lane * 8; k < KV * REP * HD; k += 256) tc::img_store8(out_img, b, k, KV * REP * HD, z);
+  } else {
+    for (int i = lane; i < KV * REP * HD; i += 32) out[(int64_t)b * ldo + i] = 0.0f;
+  }
+}
+
+template <int HD, int KV, int REP, bool SPLIT, typename KT = float>
+__global__ void __launch_bounds__(128) attn_warp_kernel(
+    const float* __restrict__ qb, int ldq, const KT* __restrict__ kc, const KT* __restrict__ vc,
+    int64_t cstride, int64_t layer_off, const int32_t* __restrict__ len, int len_add,
+    const int32_t* __restrict__ flags, float* __restrict__ out, int ldo, int S, float denom, int n,
+    uint8_t* __restrict__ out_img, const int32_t* __restrict__ seq) {
+  constexpr int C = HD / 16;
+  constexpr int R = KV * C;
+  constexpr int PPW = 32 / R;
+  constexpr int ROW = KV * HD;  // floats per cached row
+  static_assert(32 % R == 0, "a row must map onto a power-of-two lane group");
+  grid_dep_launch();
+  grid_dep_wait();
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= n) return;
+  const int r = lane % R, kvh = r / C, chunk = r % C;
+  int T = len[b] + len_add;
+  T = T > S ? S : T;
+  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
+    attn_rows_zero<HD, KV, REP, SPLIT>(b, lane, out, ldo, out_img);
+    return;
+  }
+  float q[REP][16];
+#pragma unroll
+  for (int j = 0; j < REP; ++j) {
+    const float4* qp = reinterpret_cast<const float4*>(qb + (int64_t)b * ldq + (kvh * REP + j) * HD + chunk * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = qp[i];
+      q[j][4 * i] = v.x; q[j][4 * i + 1] = v.y; q[j][4 * i + 2] = v.z; q[j][4 * i + 3] = v.w;
+    }
+  }
+  const int64_t crow = seq ? seq[b] : b;
+  const KT* kb = kc + crow * cstride + layer_off + r * 16;
+  const KT* vb = vc + crow * cstride + layer_off + r * 16;
+  const int t_lane = lane / R;
+  float4 kn[4], vn[4];
+  if (t_lane < T) {
+    load_kv16(kb + (int64_t)t_lane * ROW, kn);
+    load_kv16(vb + (int64_t)t_lane * ROW, vn);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) kn[i] = vn[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  attn_rows_body<HD, KV, REP, SPLIT, KT>(q, kn, vn, kb, vb, T, b, lane, denom, out, ldo, out_img);
 }
 
 // Causal attention of the token rows of a batched prefill (rows of prompt p
@@ -932,6 +957,15 @@ __global__ void __launch_bounds__(kPromptThreads) attn_prompt_kernel(
   }
 }
 
+// The per-sequence kernel for one instantiation.
+template <int HD, int KV, int REP, bool SPLIT, typename KT>
+static void launch_rows(int n, cudaStream_t st, bool pdl, const float* qb, int ldq, const KT* kc, const KT* vc,
+                        int64_t cstride, int64_t layer_off, const int32_t* len, int len_add, const int32_t* flags,
+                        float* out, int ldo, int S, float denom, uint8_t* out_img, const int32_t* seq) {
+  (void)launch_k(attn_warp_kernel<HD, KV, REP, SPLIT, KT>, dim3((n + 3) / 4), dim3(128), 0, st, pdl, qb, ldq, kc,
+                 vc, cstride, layer_off, len, len_add, flags, out, ldo, S, denom, n, out_img, seq);
+}
+
 // Launch the streaming kernel when the shape has an instantiation; returns
 // false to fall back to the per-head kernel.
 static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st, const float* qb, int ldq,
@@ -946,21 +980,19 @@ static bool launch_attn_rows(int hd, int KV, int rep, dim3 grid, cudaStream_t st
   const __half* vh = static_cast<const __half*>(vc);
 #define Q6W_ROWS(HDV, KVV, REPV)                                                                           \
   if (hd == HDV && KV == KVV && rep == REPV) {                                                             \
-    const dim3 nb(((int)grid.x + 3) / 4), bl(128);                                                         \
+    const int n = (int)grid.x;                                                                             \
     if (kv_half && out_img)                                                                                \
-      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, true, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,    \
-                   cstride, layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, out_img, seq); \
+      launch_rows<HDV, KVV, REPV, true, __half>(n, st, pdl, qb, ldq, kh, vh, cstride, layer_off, len,      \
+                                                len_add, flags, out, ldo, S, denom, out_img, seq);         \
     else if (kv_half)                                                                                      \
-      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, false, __half>, nb, bl, 0, st, pdl, qb, ldq, kh, vh,   \
-                   cstride, layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x,               \
-                   (uint8_t*)nullptr, seq);                                                                \
+      launch_rows<HDV, KVV, REPV, false, __half>(n, st, pdl, qb, ldq, kh, vh, cstride, layer_off, len,     \
+                                                 len_add, flags, out, ldo, S, denom, nullptr, seq);        \
     else if (out_img)                                                                                      \
-      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, true>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,   \
-                   layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, out_img, seq);         \
+      launch_rows<HDV, KVV, REPV, true, float>(n, st, pdl, qb, ldq, kf, vf, cstride, layer_off, len,       \
+                                               len_add, flags, out, ldo, S, denom, out_img, seq);          \
     else                                                                                                   \
-      (void)launch_k(attn_warp_kernel<HDV, KVV, REPV, false>, nb, bl, 0, st, pdl, qb, ldq, kf, vf, cstride,  \
-                   layer_off, len, len_add, flags, out, ldo, S, denom, (int)grid.x, (uint8_t*)nullptr,     \
-                   seq);                                                                                   \
+      launch_rows<HDV, KVV, REPV, false, float>(n, st, pdl, qb, ldq, kf, vf, cstride, layer_off, len,      \
+                                                len_add, flags, out, ldo, S, denom, nullptr, seq);         \
     return true;                                                                                           \
   }
   Q6W_ROWS(16, 1, 1) Q6W_ROWS(16, 2, 1) Q6W_ROWS(16, 4, 1) Q6W_ROWS(16, 8, 1)
