@@ -825,12 +825,12 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
 // 0 .. last row) pass through shared memory once, in tiles of kPT positions,
 // instead of once per row.  Thread = (query row, q head of the group): q and
 // the output accumulator in registers, keys read as shared-memory broadcasts.
-// Per key the arithmetic is the decode kernel's (dot as 16-element FMA chains
-// per chunk added pairwise, score = dot / denom, online softmax with expf,
-// output acc / l); keys are taken in position order, so results agree with
-// the decode path to rounding (not bit for bit: the decode kernel splits keys
-// over lane groups).  Two keys go through the dot products at once, as
-// packed FP32x2 FMAs.
+// Per key: the dot product as two FP32x2 FMA chains over dimension pairs
+// (no register repacking: q and the key rows are read as aligned pairs), score
+// = dot / denom, online softmax with expf, the accumulator updated with
+// FP32x2 FMAs, output acc / l.  Keys go in position order; results agree
+// with the decode path (whose dot is one FMA chain per 16 dimensions and whose
+// keys are split over lane groups) to rounding.
 constexpr int kPromptThreads = 128;
 constexpr int kPT = 64;  // key positions per shared-memory tile
 
@@ -841,7 +841,6 @@ __global__ void __launch_bounds__(kPromptThreads) attn_prompt_kernel(
     int64_t rows, const int32_t* __restrict__ flags, float denom, float* __restrict__ out, int ldo,
     uint8_t* __restrict__ out_img) {
   constexpr int kRB = kPromptThreads / REP;  // query rows per CTA
-  constexpr int C = HD / 16;
   __shared__ __align__(16) float sk[kPT * HD];
   __shared__ __align__(16) float sv[kPT * HD];
   grid_dep_launch();
@@ -858,15 +857,16 @@ __global__ void __launch_bounds__(kPromptThreads) attn_prompt_kernel(
   const bool act = inside && !(flags[row] & SEQ_INVALID);
   const int K = KV * REP * HD;
   const int h = g * REP + j;
-  float q[HD];
+  float2 q2[HD / 2];
 #pragma unroll
-  for (int c = 0; c < HD; ++c) q[c] = 0.0f;
+  for (int c = 0; c < HD / 2; ++c) q2[c] = make_float2(0.0f, 0.0f);
   if (act) {
     const float4* qp = reinterpret_cast<const float4*>(qb + row * ldq + h * HD);
 #pragma unroll
     for (int c = 0; c < HD / 4; ++c) {
       const float4 v = qp[c];
-      q[4 * c] = v.x; q[4 * c + 1] = v.y; q[4 * c + 2] = v.z; q[4 * c + 3] = v.w;
+      q2[2 * c] = make_float2(v.x, v.y);
+      q2[2 * c + 1] = make_float2(v.z, v.w);
     }
   }
   float2 acc[HD / 2];
@@ -889,50 +889,35 @@ __global__ void __launch_bounds__(kPromptThreads) attn_prompt_kernel(
     }
     __syncthreads();
     const int mine = act ? min(tn, i + 1 - t0) : 0;  // keys <= i in this tile
-    for (int tt = 0; tt < mine; tt += 2) {
-      const bool two = tt + 1 < mine;
-      const float* k0 = sk + tt * HD;
-      const float* k1 = two ? k0 + HD : k0;
-      float2 dc[C];
+    for (int tt = 0; tt < mine; ++tt) {
+      // q.k over dimension pairs: two FP32x2 FMA chains (dims 4c, 4c+1 and 4c+2, 4c+3), then their lanes added
+      const float* kr = sk + tt * HD;
+      float2 da = make_float2(0.0f, 0.0f), db = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        float2 d = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int u = 0; u < 16; u += 4) {
-          const float4 a = *reinterpret_cast<const float4*>(k0 + 16 * c + u);
-          const float4 b = *reinterpret_cast<const float4*>(k1 + 16 * c + u);
-          d = __ffma2_rn(make_float2(q[16 * c + u], q[16 * c + u]), make_float2(a.x, b.x), d);
-          d = __ffma2_rn(make_float2(q[16 * c + u + 1], q[16 * c + u + 1]), make_float2(a.y, b.y), d);
-          d = __ffma2_rn(make_float2(q[16 * c + u + 2], q[16 * c + u + 2]), make_float2(a.z, b.z), d);
-          d = __ffma2_rn(make_float2(q[16 * c + u + 3], q[16 * c + u + 3]), make_float2(a.w, b.w), d);
-        }
-        dc[c] = d;
+      for (int c = 0; c < HD / 4; ++c) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * c);
+        da = __ffma2_rn(q2[2 * c], make_float2(k4.x, k4.y), da);
+        db = __ffma2_rn(q2[2 * c + 1], make_float2(k4.z, k4.w), db);
       }
+      const float2 d = __fadd2_rn(da, db);
+      const float dot = __fadd_rn(d.x, d.y);
+      const float sc = pow2 ? dot * inv : __fdiv_rn(dot, denom);
+      if (sc > m) {
+        const float cf = expf(m - sc);
+        l *= cf;
 #pragma unroll
-      for (int w = 1; w < C; w <<= 1)  // the decode kernel's butterfly order
+        for (int c = 0; c < HD / 2; ++c) acc[c] = __fmul2_rn(acc[c], make_float2(cf, cf));
+        m = sc;
+      }
+      const float pr = expf(sc - m);
+      l += pr;
+      const float2 p2 = make_float2(pr, pr);
+      const float* vr = sv + tt * HD;
 #pragma unroll
-        for (int c = 0; c < C; c += 2 * w) dc[c] = __fadd2_rn(dc[c], dc[c + w]);
-      const float d2[2] = {dc[0].x, dc[0].y};
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        if (s == 1 && !two) break;
-        const float sc = pow2 ? d2[s] * inv : __fdiv_rn(d2[s], denom);
-        if (sc > m) {
-          const float cf = expf(m - sc);
-          l *= cf;
-#pragma unroll
-          for (int c = 0; c < HD / 2; ++c) acc[c] = __fmul2_rn(acc[c], make_float2(cf, cf));
-          m = sc;
-        }
-        const float pr = expf(sc - m);
-        l += pr;
-        const float* vr = sv + (tt + s) * HD;
-#pragma unroll
-        for (int c = 0; c < HD / 4; ++c) {
-          const float4 v = *reinterpret_cast<const float4*>(vr + 4 * c);
-          acc[2 * c] = __ffma2_rn(make_float2(pr, pr), make_float2(v.x, v.y), acc[2 * c]);
-          acc[2 * c + 1] = __ffma2_rn(make_float2(pr, pr), make_float2(v.z, v.w), acc[2 * c + 1]);
-        }
+      for (int c = 0; c < HD / 4; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(vr + 4 * c);
+        acc[2 * c] = __ffma2_rn(p2, make_float2(v.x, v.y), acc[2 * c]);
+        acc[2 * c + 1] = __ffma2_rn(p2, make_float2(v.z, v.w), acc[2 * c + 1]);
       }
     }
   }
