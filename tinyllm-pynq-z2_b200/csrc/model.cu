@@ -778,7 +778,6 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
     uint8_t* __restrict__ out_img, const int32_t* __restrict__ seq) {
   constexpr int C = HD / 16;
   constexpr int R = KV * C;
-  constexpr int PPW = 32 / R;
   constexpr int ROW = KV * HD;  // floats per cached row
   static_assert(32 % R == 0, "a row must map onto a power-of-two lane group");
   grid_dep_launch();

@@ -184,6 +184,58 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 16-column TMEM loads in flight together, one wait (the wait names the
+// destination registers, so no use of them is scheduled before it).
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, float (&va)[16], uint32_t tb, float (&vb)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(ta));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[16 + i]);
+  }
+}
+
+// Two 32-column TMEM loads in flight together, one wait (as tmem_ld16x2).
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, float (&va)[32], uint32_t tb, float (&vb)[32]) {
+  uint32_t r[64];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(ta));
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+               : "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]), "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[32 + i]);
+  }
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -493,47 +545,58 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       float bv = -INFINITY;
       int bi = -1;
       const int cb = half * (a.N / kParts), ce = cb + a.N / kParts;
-      for (int c0 = cb; c0 < ce; c0 += 32) {
-        float v[32];
-        tmem_ld32(lane_addr + c0, v);
+      for (int c2 = cb; c2 < ce; c2 += 64) {
+        // two 32-column chunks loaded together (one when 32 columns remain)
+        float vv[2][32];
+        const int nh = c2 + 32 < ce ? 2 : 1;
+        if (nh == 2)
+          tmem_ld32x2(lane_addr + c2, vv[0], lane_addr + c2 + 32, vv[1]);
+        else
+          tmem_ld32(lane_addr + c2, vv[0]);
         if (!live) continue;
-        const int r0 = nt * a.N + c0;
-        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 sc = s4[i];
-          v[4 * i] = __fmul_rn(v[4 * i], sc.x);
-          v[4 * i + 1] = __fmul_rn(v[4 * i + 1], sc.y);
-          v[4 * i + 2] = __fmul_rn(v[4 * i + 2], sc.z);
-          v[4 * i + 3] = __fmul_rn(v[4 * i + 3], sc.w);
-        }
-        if (ep.y) {
-          float4* y = reinterpret_cast<float4*>(ep.y + m * ep.ldy + r0);
+        for (int hh = 0; hh < 2; ++hh) {
+          if (hh >= nh) break;
+          float (&v)[32] = vv[hh];
+          const int c0 = c2 + 32 * hh;
+          const int r0 = nt * a.N + c0;
+          const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-        if (dump) {
-          float4* y = reinterpret_cast<float4*>(ep.step_logits + (m * ep.new_tokens + ep.gen[m]) * ep.vocab + r0);
+          for (int i = 0; i < 8; ++i) {
+            const float4 sc = s4[i];
+            v[4 * i] = __fmul_rn(v[4 * i], sc.x);
+            v[4 * i + 1] = __fmul_rn(v[4 * i + 1], sc.y);
+            v[4 * i + 2] = __fmul_rn(v[4 * i + 2], sc.z);
+            v[4 * i + 3] = __fmul_rn(v[4 * i + 3], sc.w);
+          }
+          if (ep.y) {
+            float4* y = reinterpret_cast<float4*>(ep.y + m * ep.ldy + r0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-        if (mask) {
-          for (int s = 0; s < ep.n_stop; ++s) {
-            const int k = ep.stop_ids[s] - r0;
-            if (k >= 0 && k < 32) {
+            for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+          if (dump) {
+            float4* y = reinterpret_cast<float4*>(ep.step_logits + (m * ep.new_tokens + ep.gen[m]) * ep.vocab + r0);
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i == k) v[i] = -INFINITY;
+            for (int i = 0; i < 8; ++i) y[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+          if (mask) {
+            for (int s = 0; s < ep.n_stop; ++s) {
+              const int k = ep.stop_ids[s] - r0;
+              if (k >= 0 && k < 32) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i == k) v[i] = -INFINITY;
+              }
             }
           }
-        }
-        // first maximum in increasing column order (torch.argmax's tie rule)
+          // first maximum in increasing column order (torch.argmax's tie rule)
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (v[i] > bv || bi < 0) {
-            bv = v[i];
-            bi = r0 + i;
-          }
+          for (int i = 0; i < 32; ++i)
+            if (v[i] > bv || bi < 0) {
+              bv = v[i];
+              bi = r0 + i;
+            }
+        }
       }
       if (live && bi >= 0) atomicMax(ep.keys + m, argmax_key(bv, bi));
     } else if (EPI == TEPI_STORE) {
@@ -717,8 +780,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       for (int cc = 0; cc < hq; cc += 16) {
         const int c0 = half * hq + cc;
         float va[16], vb[16];
-        tmem_ld16(lane_addr + c0, va);
-        tmem_ld16(lane_addr + H + c0, vb);
+        tmem_ld16x2(lane_addr + c0, va, lane_addr + H + c0, vb);
         if (!live) continue;
 #pragma unroll
         for (int k0 = 0; k0 < 16; k0 += 8) {
