@@ -786,12 +786,13 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= n) return;
   const int r = lane % R, kvh = r / C, chunk = r % C;
-  int T = len[b] + len_add;
-  T = T > S ? S : T;
-  if ((flags && (flags[b] & SEQ_INVALID)) || T <= 0) {
-    attn_rows_zero<HD, KV, REP, SPLIT>(b, lane, out, ldo, out_img);
-    return;
-  }
+  const int t_lane = lane / R;
+  // The length, the query and (when the cache row is the sequence's own) the
+  // first pass's K/V rows are all requested before any of them is used: one
+  // memory round trip instead of two.  Those rows lie inside the cache for
+  // any length (t_lane < S) and are replaced by zeros below when past it.
+  const int len_b = len[b];
+  const int flag_b = flags ? flags[b] : 0;
   float q[REP][16];
 #pragma unroll
   for (int j = 0; j < REP; ++j) {
@@ -805,11 +806,23 @@ __global__ void __launch_bounds__(128) attn_warp_kernel(
   const int64_t crow = seq ? seq[b] : b;
   const KT* kb = kc + crow * cstride + layer_off + r * 16;
   const KT* vb = vc + crow * cstride + layer_off + r * 16;
-  const int t_lane = lane / R;
   float4 kn[4], vn[4];
-  if (t_lane < T) {
+  const bool early = !seq && t_lane < S;
+  if (early) {
     load_kv16(kb + (int64_t)t_lane * ROW, kn);
     load_kv16(vb + (int64_t)t_lane * ROW, vn);
+  }
+  int T = len_b + len_add;
+  T = T > S ? S : T;
+  if ((flag_b & SEQ_INVALID) || T <= 0) {
+    attn_rows_zero<HD, KV, REP, SPLIT>(b, lane, out, ldo, out_img);
+    return;
+  }
+  if (t_lane < T) {
+    if (!early) {
+      load_kv16(kb + (int64_t)t_lane * ROW, kn);
+      load_kv16(vb + (int64_t)t_lane * ROW, vn);
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < 4; ++i) kn[i] = vn[i] = make_float4(0.f, 0.f, 0.f, 0.f);
