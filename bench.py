@@ -554,9 +554,22 @@ def b1_latency(model, prompt, new_tokens, stream, reps=5):
         dec.append(e1.elapsed_time(e2) / 1e3)
     t, d = statistics.median(tot), statistics.median(dec)
     steps = len(prompt) + new_tokens - 1
+    # Roofline of a model step: the weights it uses (1,178,624 B: packed rows, scales, tied head, norms,
+    # one embedding row) plus the K/V rows read (2560 B a position) and written, averaged over the
+    # request's steps; against the measured L2 copy rate and the HBM copy peak.  The cluster kernel
+    # keeps the weights in shared memory, so these fractions are small by design: the step is
+    # latency-bound (about 30 dependent phases a step).
+    kv_row = 2 * model.n_kv_heads * model.head_dim * 4 * model.args.n_layers
+    step_bytes = 1_178_624 + kv_row * (sum(p + 1 for p in range(steps)) / steps + 1)
+    ach = step_bytes / (t / steps) / 1e9
+    l2 = l2_copy_gbs(dev, stream)
+    hbm, kind = measured_peaks()
     return {"workload": f"B=1 greedy, {len(prompt)}-token prompt + {new_tokens} tokens, tiny model",
             "request_tok_s": round(new_tokens / t, 1), "decode_tok_s": round(new_tokens / d, 1),
-            "us_per_model_step": round(t / steps * 1e6, 2), "prefill_ms": round((t - d) * 1e3, 3)}
+            "us_per_model_step": round(t / steps * 1e6, 2), "prefill_ms": round((t - d) * 1e3, 3),
+            "roofline": {"bound": "latency", "bytes_per_step": int(step_bytes), "achieved_gbs": round(ach, 1),
+                         "l2_copy_gbs": l2, "frac_of_l2": round(ach / l2, 4), "hbm_gbs": hbm,
+                         "frac_of_hbm": round(ach / hbm, 4), "peak_kind": f"{kind} hbm_gbs; L2 copy measured here"}}
 
 
 def scaled_gemv(dev, stream, reps=10):
