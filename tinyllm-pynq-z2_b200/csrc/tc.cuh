@@ -257,13 +257,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 enum { TEPI_QKV = 0, TEPI_RESNORM = 1, TEPI_GLU = 2, TEPI_VOCAB = 3, TEPI_STORE = 4 };
 
-// Threads per CTA.  The weight expansion and the SwiGLU / argmax epilogues
-// are latency-bound at one CTA per SM, so those kernels run 16 warps (each
-// TMEM lane quadrant read by four warps, a quarter of the columns each); the
-// QKV and residual + RMSNorm epilogues hold whole row blocks in registers
-// and keep 8 warps.
+// Threads per CTA.  The weight expansion and the SwiGLU / argmax / residual
+// + RMSNorm epilogues are latency-bound at one CTA per SM, so those kernels
+// run 16 warps (each TMEM lane quadrant read by four warps, a quarter of the
+// columns each; a warp takes 8 rows of the residual pass instead of 16); the
+// QKV epilogue keeps 8 warps.
 __host__ __device__ constexpr int threads_for(int epi) {
-  return (epi == TEPI_GLU || epi == TEPI_VOCAB) ? 512 : kThreads;
+  return (epi == TEPI_GLU || epi == TEPI_VOCAB || epi == TEPI_RESNORM) ? 512 : kThreads;
 }
 
 // Rows per N tile of the plain linear (TEPI_STORE) on this kernel, or 0 when
@@ -444,7 +444,8 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       }
     }
     // RESNORM: the residual rows of this thread's passes and its norm weights.
-    constexpr int kPass = kM / 16;  // at most 8 passes of 2 rows per warp (4 rows in pair mode)
+    constexpr int kRPW = kM / (NT / 32);  // rows of the residual pass per warp: 16 (8 warps) or 8 (16)
+    constexpr int kPass = kRPW / 2;       // at most this many passes of 2 rows (4 in pair mode)
     float4 ox[kPass][2];
     float gw[8];
     if (EPI == TEPI_RESNORM) {
@@ -452,12 +453,12 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       const int lpr = a.N >> 3, rpi = 32 / lpr;
       const int sub = lane / lpr, cb = 8 * (lane % lpr);
       const int col = nt * a.N + cb;
-      const int npass = (kM / 8) / rpi;
+      const int npass = kRPW / rpi;
 #pragma unroll
       for (int i = 0; i < 8; ++i) gw[i] = __ldg(a.gnorm + col + i);
 #pragma unroll
       for (int i = 0; i < kPass; ++i) {
-        const int64_t mr = (int64_t)mt * kM + 16 * warp + rpi * i + sub;
+        const int64_t mr = (int64_t)mt * kM + kRPW * warp + rpi * i + sub;
         const float4* xr = reinterpret_cast<const float4*>(a.x + mr * 128 + col);
         const bool in = i < npass && mr < a.n;
         ox[i][0] = in ? xr[0] : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -688,17 +689,17 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
     } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim, or N == 64 per CTA of a pair (a.pair)
       // Two passes through shared memory (sB: the weights are consumed once the
       // MMAs are done), so every global access is row-contiguous.
-      // E1: this thread's row (TMEM lane) and columns (N/2)*half.., scaled,
+      // E1: this thread's row (TMEM lane) and columns (N/kParts)*part.., scaled,
       // into sB as float4 unit c4 of row r at r*32 + (c4 ^ (r & 7)).
       float4* st4 = reinterpret_cast<float4*>(sB);
-      const int hn = a.N >> 1;
-      for (int cc = 0; cc < hn; cc += 32) {
+      const int hn = a.N / kParts;
+      for (int cc = 0; cc < hn; cc += 16) {
         const int c0 = half * hn + cc;
-        float v[32];
-        tmem_ld32(lane_addr + c0, v);
+        float v[16];
+        tmem_ld16(lane_addr + c0, v);
         const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const float4 sc = s4[i];
           st4[row * 32 + (((c0 >> 2) + i) ^ (row & 7))] =
               make_float4(__fmul_rn(v[4 * i], sc.x), __fmul_rn(v[4 * i + 1], sc.y), __fmul_rn(v[4 * i + 2], sc.z),
@@ -714,14 +715,14 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       const int lpr = a.N >> 3, rpi = 32 / lpr;  // lanes per row, rows per warp pass
       const int sub = lane / lpr, cl8 = lane % lpr, cb = 8 * cl8;
       const int col = nt * a.N + cb;  // column of x and of the image
-      const int npass = (kM / 8) / rpi;
+      const int npass = kRPW / rpi;
       // ox (the residual rows of all passes) and gw were loaded at the item's start
       float xk[kPass][8];
       float ssk[kPass];
 #pragma unroll
       for (int i = 0; i < kPass; ++i) {
         ssk[i] = 0.0f;
-        const int r = 16 * warp + rpi * i + sub;
+        const int r = kRPW * warp + rpi * i + sub;
         const int64_t mr = (int64_t)mt * kM + r;
         const bool lv = i < npass && mr < a.n;  // uniform over the lanes of the row
 #pragma unroll
@@ -756,7 +757,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
 #pragma unroll
         for (int i = 0; i < kPass; ++i) {
           if (i < npass) {
-            const int r = 16 * warp + rpi * i + sub;
+            const int r = kRPW * warp + rpi * i + sub;
             ssk[i] = nt == 0 ? __fadd_rn(ssk[i], peer[r]) : __fadd_rn(peer[r], ssk[i]);
           }
         }
@@ -765,7 +766,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       }
 #pragma unroll
       for (int i = 0; i < kPass; ++i) {
-        const int64_t mr = (int64_t)mt * kM + 16 * warp + rpi * i + sub;
+        const int64_t mr = (int64_t)mt * kM + kRPW * warp + rpi * i + sub;
         if (i < npass && mr < a.n) {
           const float rstd = rms_scale(ssk[i], 128, a.eps);
           float u8[8];
