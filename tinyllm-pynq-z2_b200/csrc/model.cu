@@ -365,6 +365,16 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
   const KT* kb = kc + crow * cstride + layer_off + g * HD;
   const KT* vb = vc + crow * cstride + layer_off + g * HD;
   if (tid < HD) sq[tid] = qb[(int64_t)b * ldq + h * HD + tid];
+  // this thread's first V rows of the V pass, requested now so their latency
+  // hides behind the score phase
+  const int cq = tid % CQ, grp = tid / CQ;
+  constexpr int kVP = 4;
+  float4 vpre[kVP];
+#pragma unroll
+  for (int i = 0; i < kVP; ++i) {
+    const int t = grp + i * G;
+    vpre[i] = t < T ? load_kv4(vb + (int64_t)t * kvr + 4 * cq) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   __syncthreads();
   float mx = -INFINITY;
   for (int t = tid; t < T; t += 256) {
@@ -401,9 +411,19 @@ __global__ void __launch_bounds__(256) attn_head_kernel(
   sum = 0.0f;
 #pragma unroll
   for (int w = 0; w < 8; ++w) sum += red[8 + w];
-  const int cq = tid % CQ, grp = tid / CQ;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int t = grp; t < T; t += G) {
+#pragma unroll
+  for (int i = 0; i < kVP; ++i) {  // the prefetched rows, in position order
+    const int t = grp + i * G;
+    if (t < T) {
+      const float wt = __fdiv_rn(sp[t], sum);
+      acc.x = fmaf(wt, vpre[i].x, acc.x);
+      acc.y = fmaf(wt, vpre[i].y, acc.y);
+      acc.z = fmaf(wt, vpre[i].z, acc.z);
+      acc.w = fmaf(wt, vpre[i].w, acc.w);
+    }
+  }
+  for (int t = grp + kVP * G; t < T; t += G) {
     const float wt = __fdiv_rn(sp[t], sum);
     const float4 v4 = load_kv4(vb + (int64_t)t * kvr + 4 * cq);
     acc.x = fmaf(wt, v4.x, acc.x);
