@@ -1307,10 +1307,10 @@ static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st,
   cfg.attrs = attr;
   cudaError_t e;
   if (epi == tc::TEPI_RESNORM && a.pair) {
-    // one item per CTA, the two column halves of an M tile in one 2-CTA cluster
+    // one item per CTA, the column blocks of an M tile in one cluster
     cfg.gridDim = dim3((unsigned)items);
     attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.x = (unsigned)a.pair;
     attr[na].val.clusterDim.y = 1;
     attr[na].val.clusterDim.z = 1;
     ++na;
@@ -1330,15 +1330,31 @@ static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st,
   return Q6W_OK;
 }
 
-// RESNORM tiles (dim 128): when every M tile can have two CTAs at once, its
-// two 64-column halves run as a 2-CTA cluster (twice the CTAs, half the
-// epilogue each); otherwise one CTA takes all 128 columns.
+// RESNORM tiles (dim 128): the 128 columns of an M tile split into P blocks
+// of 128 / P columns, one CTA each, in one P-CTA cluster (P times the CTAs,
+// 1/P of the epilogue each), with P = 4 when every M tile can have four CTAs
+// at once (up to 37 tiles, 4736 sequences), else 2 when it can have two;
+// otherwise one CTA takes all 128 columns.
 static void tc_resnorm_tiles(tc::TcArgs& a, int n, int sms) {
   const int m_tiles = (n + tc::kM - 1) / tc::kM;
-  const bool pair = 2 * m_tiles <= sms;
-  a.N = pair ? 64 : 128;
-  a.n_tiles = pair ? 2 : 1;
-  a.pair = pair ? 1 : 0;
+  const int P = 4 * m_tiles <= sms ? 4 : 2 * m_tiles <= sms ? 2 : 1;
+  a.N = 128 / P;
+  a.n_tiles = P;
+  a.pair = P > 1 ? P : 0;
+}
+
+// Rows per N tile of the QKV and SwiGLU linears.  Few M tiles (a small
+// batch) leave most SMs idle at the default tiles, so the tiles narrow to 64
+// rows (QKV) or 32 W1 + 32 W3 rows (SwiGLU) while the items still fit one
+// CTA each on the SMs; each item's epilogue is then half as long.
+static int tc_qkv_rows_per_tile(int n, int qkv_rows, int sms) {
+  const int m_tiles = (n + tc::kM - 1) / tc::kM;
+  if (m_tiles * (qkv_rows / 64) <= sms) return 64;
+  return qkv_rows % 128 == 0 ? 128 : qkv_rows;
+}
+static int tc_glu_rows_per_tile(int n, int hid, int sms) {
+  const int m_tiles = (n + tc::kM - 1) / tc::kM;
+  return m_tiles * (hid / 32) <= sms ? 64 : 128;
 }
 
 static int32_t tc_set_attrs() {
@@ -1383,9 +1399,10 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.q0 = L.wq.packed; a.q1 = L.wk.packed; a.q2 = L.wv.packed;
       a.s0 = L.wq.scales; a.s1 = L.wk.scales; a.s2 = L.wv.scales;
       a.end0 = dim; a.end1 = dim + kvr;
-      // two tiles of 128 rows (q | k v) give twice the CTAs when the rows divide
+      // two tiles of 128 rows (q | k v) give twice the CTAs when the rows
+      // divide; tiles of 64 rows at small batches
       const int qkv_rows = dim + 2 * kvr;
-      a.N = qkv_rows % 128 == 0 ? 128 : qkv_rows;
+      a.N = tc_qkv_rows_per_tile(n, qkv_rows, M->sm_count);
       a.n_tiles = qkv_rows / a.N;
       a.ep.qbuf = w.qb; a.ep.ldq = dim;
       a.ep.kc = kc; a.ep.vc = vc; a.ep.cache_stride = cstride; a.ep.layer_off = layer_off;
@@ -1419,10 +1436,11 @@ static int32_t enqueue_step_tc(const q6w_model* M, int n, const Work& w, float* 
       a.a_img = w.xs_img;
       a.K = dim;
       a.q0 = L.w1.packed; a.s0 = L.w1.scales; a.q1 = L.w3.packed; a.s1 = L.w3.scales;
-      // tiles of 64 W1 + 64 W3 rows: more, smaller items spread over the SMs
-      // (each CTA keeps its activation tile across consecutive items)
-      a.N = 128;
-      a.n_tiles = hid / 64;
+      // tiles of 64 W1 + 64 W3 rows (32 + 32 at small batches): more, smaller
+      // items spread over the SMs (each CTA keeps its activation tile across
+      // consecutive items)
+      a.N = tc_glu_rows_per_tile(n, hid, M->sm_count);
+      a.n_tiles = hid / (a.N / 2);
       a.out_img = w.hs_img; a.out_K = hid;
       if ((rc = tc_launch(tc::TEPI_GLU, a, M->sm_count, st, w.pdl))) return rc;
     }

@@ -24,10 +24,12 @@
 //
 // Tiles.  An item is (128-sequence M tile, N-row weight tile).  QKV uses two
 // 128-row tiles (q | k v) when the rows divide, GLU tiles of 64 W1 + 64 W3
-// rows, VOCAB 256 rows; RESNORM needs whole rows for its RMSNorm and runs
-// each M tile either in one CTA (N = 128) or, when every M tile can have two
-// CTAs at once, as a 2-CTA cluster of 64-column halves that add their
-// per-row sums of squares through distributed shared memory.
+// rows, VOCAB 256 rows; at small batches (few M tiles) QKV and GLU narrow to
+// 64-row tiles so more SMs take part.  RESNORM needs whole rows for its
+// RMSNorm and runs each M tile either in one CTA (N = 128) or, when every M
+// tile can have two (four) CTAs at once, as a 2-CTA (4-CTA) cluster of 64-
+// (32-) column blocks that add their per-row sums of squares through
+// distributed shared memory.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -236,6 +238,42 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t ta, float (&va)[32], uint32
   }
 }
 
+// Two 8-column TMEM loads in flight together, one wait (as tmem_ld16x2).
+__device__ __forceinline__ void tmem_ld8x2(uint32_t ta, float (&va)[8], uint32_t tb, float (&vb)[8]) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(ta));
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                 "=r"(r[15])
+               : "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[8 + i]);
+  }
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -290,7 +328,7 @@ struct TcArgs {
   int32_t end0, end1;  // QKV: virtual-row ends of wq and wk
   int32_t N;           // rows per N tile (64, 128 or 256)
   int32_t n_tiles;     // N tiles per M tile
-  int32_t pair;        // RESNORM: the two 64-column tiles of an M tile run as a 2-CTA cluster
+  int32_t pair;        // RESNORM: 0, or the cluster size (2 or 4) whose CTAs take the N-column blocks of an M tile
   // epilogue
   float* x;            // RESNORM: residual stream [n, 128] (read + written)
   const float* gnorm;  // RESNORM: norm weight applied to the new x for the next image
@@ -686,14 +724,27 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
         }
         __syncthreads();  // the next block reuses sB
       }
-    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim, or N == 64 per CTA of a pair (a.pair)
+    } else if (EPI == TEPI_RESNORM) {  // N == 128 == dim, or N == 128 / a.pair per CTA of a cluster
       // Two passes through shared memory (sB: the weights are consumed once the
       // MMAs are done), so every global access is row-contiguous.
       // E1: this thread's row (TMEM lane) and columns (N/kParts)*part.., scaled,
       // into sB as float4 unit c4 of row r at r*32 + (c4 ^ (r & 7)).
       float4* st4 = reinterpret_cast<float4*>(sB);
       const int hn = a.N / kParts;
-      for (int cc = 0; cc < hn; cc += 16) {
+      if (hn == 8) {  // N == 32 (a CTA of a 4-CTA cluster) at 16 warps: 8 columns a thread
+        const int c0 = half * 8;
+        float v[8];
+        tmem_ld8(lane_addr + c0, v);
+        const float4* s4 = reinterpret_cast<const float4*>(sscale + c0);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float4 sc = s4[i];
+          st4[row * 32 + (((c0 >> 2) + i) ^ (row & 7))] =
+              make_float4(__fmul_rn(v[4 * i], sc.x), __fmul_rn(v[4 * i + 1], sc.y), __fmul_rn(v[4 * i + 2], sc.z),
+                          __fmul_rn(v[4 * i + 3], sc.w));
+        }
+      }
+      for (int cc = 0; hn >= 16 && cc < hn; cc += 16) {
         const int c0 = half * hn + cc;
         float v[16];
         tmem_ld16(lane_addr + c0, v);
@@ -748,17 +799,33 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
         if (a.pair && i < npass && cl8 == 0) s_ssp[r] = ss;
       }
       if (a.pair) {
-        // both halves of every row: the partial sums meet through distributed
-        // shared memory; the second barrier (arrive here, wait before the CTA
-        // exits) keeps this CTA's array alive until the peer has read it
+        // every column block of every row: the a.pair partial sums meet
+        // through distributed shared memory and are added in rank order (the
+        // cluster rank is nt); the second barrier (arrive here, wait before
+        // the CTA exits) keeps this CTA's array alive until the peers have
+        // read it
         cg::cluster_group cl = cg::this_cluster();
         cl.sync();
-        const float* peer = cl.map_shared_rank(s_ssp, nt ^ 1);
+        if (a.pair == 2) {
+          const float* peer = cl.map_shared_rank(s_ssp, nt ^ 1);
 #pragma unroll
-        for (int i = 0; i < kPass; ++i) {
-          if (i < npass) {
-            const int r = kRPW * warp + rpi * i + sub;
-            ssk[i] = nt == 0 ? __fadd_rn(ssk[i], peer[r]) : __fadd_rn(peer[r], ssk[i]);
+          for (int i = 0; i < kPass; ++i) {
+            if (i < npass) {
+              const int r = kRPW * warp + rpi * i + sub;
+              ssk[i] = nt == 0 ? __fadd_rn(ssk[i], peer[r]) : __fadd_rn(peer[r], ssk[i]);
+            }
+          }
+        } else {  // four blocks (every lane of a row holds the same partial sum as s_ssp)
+          const float* p0 = cl.map_shared_rank(s_ssp, 0);
+          const float* p1 = cl.map_shared_rank(s_ssp, 1);
+          const float* p2 = cl.map_shared_rank(s_ssp, 2);
+          const float* p3 = cl.map_shared_rank(s_ssp, 3);
+#pragma unroll
+          for (int i = 0; i < kPass; ++i) {
+            if (i < npass) {
+              const int r = kRPW * warp + rpi * i + sub;
+              ssk[i] = __fadd_rn(__fadd_rn(__fadd_rn(p0[r], p1[r]), p2[r]), p3[r]);
+            }
           }
         }
         cluster_arrive();
@@ -777,8 +844,20 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       }
     } else if (EPI == TEPI_GLU) {  // columns j (W1) and H + j (W3), H = N/2; this thread: j in (H/kParts)*part..
       const int H = a.N >> 1, hq = H / kParts;
+      if (hq == 8) {  // N == 64 (32 W1 + 32 W3 rows) at 16 warps: 8 columns a thread
+        const int c0 = half * 8;
+        float va[8], vb[8];
+        tmem_ld8x2(lane_addr + c0, va, lane_addr + H + c0, vb);
+        if (live) {
+          float h8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            h8[i] = swiglu(__fmul_rn(va[i], sscale[c0 + i]), __fmul_rn(vb[i], sscale[H + c0 + i]));
+          img_store8(a.out_img, m, nt * H + c0, a.out_K, h8);
+        }
+      }
 #pragma unroll 1
-      for (int cc = 0; cc < hq; cc += 16) {
+      for (int cc = 0; hq >= 16 && cc < hq; cc += 16) {
         const int c0 = half * hq + cc;
         float va[16], vb[16];
         tmem_ld16x2(lane_addr + c0, va, lane_addr + H + c0, vb);
