@@ -7,9 +7,10 @@
   last prompt position within the step tests' 2e-4, the layer-0 K/V rows bit
   for bit (the same QKV epilogue on the same embeddings), later layers within
   1e-4.
-* Programmatic dependent launch across the tensor-core step (opt-in with
-  Q6W_PDL=1 at model creation) changes only when kernels start: generated
-  tokens, step logits and caches are bit-identical to the default launches.
+* Programmatic dependent launch across the tensor-core step (Q6W_PDL=1 / 0
+  at model creation force it on / off; by default the decode step uses it at
+  small batches) changes only when kernels start: generated tokens, step
+  logits and caches are bit-identical with it on and off.
 """
 
 import os
@@ -61,15 +62,19 @@ def test_prefill_runs_prompt_attention_and_matches_step_path(tiny):
         assert float((v[i, :, :L] - vg[i, :, :L]).abs().max()) <= 1e-4, i
 
 
-def test_pdl_step_bit_identical(tiny_files, tiny):
-    os.environ["Q6W_PDL"] = "1"
+def _with_pdl(files, mode):
+    os.environ["Q6W_PDL"] = mode
     try:
-        fast = Q6WCudaTransformer.from_q6w(*tiny_files)
+        return Q6WCudaTransformer.from_q6w(*files)
     finally:
         del os.environ["Q6W_PDL"]
+
+
+def test_pdl_step_bit_identical(tiny_files):
+    on, off = _with_pdl(tiny_files, "1"), _with_pdl(tiny_files, "0")
     prompts = _prompts(300, 32, 4, 24, 4096)
-    a = fast.generate_greedy(prompts, 12, keep_logits=True)
-    b = tiny.generate_greedy(prompts, 12, keep_logits=True)
+    a = on.generate_greedy(prompts, 12, keep_logits=True)
+    b = off.generate_greedy(prompts, 12, keep_logits=True)
     assert a.sampled == b.sampled
     assert torch.equal(a.logits, b.logits)
     for i, p in enumerate(prompts):

@@ -88,7 +88,7 @@ struct q6w_model {
   bool use_b1 = false;  // shapes qualify for the single-request cluster kernel
   bool kv_half = false; // the KV cache holds FP16 (q6w_model_set_kv_dtype)
   bool use_pdec = false;  // shapes qualify for the persistent B=1 step (pdec.cuh)
-  bool use_pdl = false;   // programmatic dependent launch in the tensor-core step (opt-in: Q6W_PDL=1)
+  int pdl_mode = -1;      // programmatic dependent launch in the tensor-core step: 1 on, 0 off (Q6W_PDL), -1 by batch
   int pdec_grid = 0;
   size_t pdec_smem = 0;
   size_t b1_smem = 0;
@@ -2197,10 +2197,10 @@ extern "C" int32_t q6w_model_create(const q6w_model_desc* desc, q6w_model** out)
     const char* onp = getenv("Q6W_PDEC");
     M->use_pdec = (onp && onp[0] == '1') && major == 10 && (pdec_shapes_ok(M) || pdec_off("shapes")) &&
                   pdec_setup(M);
-    // Programmatic dependent launch across the tensor-core step measured slower on the 8192-sequence
-    // decode (116.5 against 112.1 ms a generation), as it did across the general tensor-core step.
+    // Programmatic dependent launch across the tensor-core step: Q6W_PDL=1 / 0 force it on / off;
+    // unset, the decode step uses it at small batches only (step_pdl).
     const char* pdl = getenv("Q6W_PDL");
-    M->use_pdl = pdl && pdl[0] == '1';
+    M->pdl_mode = !pdl || !pdl[0] ? -1 : pdl[0] == '1' ? 1 : 0;
   }
   *out = M;
   return Q6W_OK;
@@ -2356,6 +2356,18 @@ extern "C" int32_t q6w_forward_batch(const q6w_model* M, int32_t n, const int32_
   return Q6W_OK;
 }
 
+// Whether the decode step of n sequences launches its kernels with
+// programmatic dependencies (each kernel's setup and weight copies overlap the
+// previous kernel's tail).  Measured on the tensor-core step: faster at small
+// batches (1024 sequences 37.1 -> 35.9 ms a generation, 4096 70.2 -> 69.3 ms),
+// slower at 8192 (109.5 against 107.2-107.5 ms), so by default it is used
+// while the batch has at most sm_count / 4 M tiles, the batches that also take
+// the narrow tiles.
+static bool step_pdl(const q6w_model* M, int n) {
+  if (M->pdl_mode >= 0) return M->pdl_mode == 1;
+  return 4 * ((n + tc::kM - 1) / tc::kM) <= M->sm_count;
+}
+
 static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& w,
                             const StopSet& stop, const smp::Params* sp) {
   if (!M->cap_stream) Q6W_CUDA_TRY(cudaStreamCreateWithFlags(&M->cap_stream, cudaStreamNonBlocking));
@@ -2377,7 +2389,7 @@ static int32_t capture_step(q6w_model* M, const q6w_greedy_args* a, const Work& 
     v.ldy = M->d.vocab_size;
   }
   Work wp = w;
-  wp.pdl = M->use_pdl;
+  wp.pdl = step_pdl(M, a->n_seqs);
   int32_t st = enqueue_step(M, a->n_seqs, wp, a->k_cache, a->v_cache, a->cache_seq_stride, v,
                             M->cap_stream);
   if (st == Q6W_OK && sp) {
@@ -2487,7 +2499,7 @@ extern "C" int32_t q6w_prefill(const q6w_model* M, int32_t n_prompts, const int3
   w.plens = prompt_lens;
   w.n_prompts = n_prompts;
   w.max_len = max_prompt_len;
-  w.pdl = M->use_pdl;
+  w.pdl = M->pdl_mode == 1;
   EpiArgs none;
   memset(&none, 0, sizeof(none));
   if ((st = enqueue_step(M, rows, w, k_cache, v_cache, cache_seq_stride, none, s, false))) return st;
@@ -2557,7 +2569,7 @@ extern "C" int32_t q6w_forward_all(const q6w_model* M, int32_t n_prompts, const 
   w.plens = prompt_lens;
   w.n_prompts = n_prompts;
   w.max_len = max_prompt_len;
-  w.pdl = M->use_pdl;
+  w.pdl = M->pdl_mode == 1;
   // every row through the layers and the vocab head (final RMSNorm + tied embedding): the logits of
   // every position, row off[i] + j for position j of prompt i
   EpiArgs v;
