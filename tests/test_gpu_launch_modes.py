@@ -7,6 +7,10 @@
   last prompt position within the step tests' 2e-4, the layer-0 K/V rows bit
   for bit (the same QKV epilogue on the same embeddings), later layers within
   1e-4.
+* The decode attention's two-pass prefetch (Q6W_ATTN_DEEP=1 / 0 force it
+  on / off; by default it is used at small batches) reads the same positions
+  in the same order per lane: generations are bit-identical with it on and
+  off.
 * Programmatic dependent launch across the tensor-core step (Q6W_PDL=1 / 0
   at model creation force it on / off; by default the decode step uses it at
   small batches) changes only when kernels start: generated tokens, step
@@ -62,16 +66,34 @@ def test_prefill_runs_prompt_attention_and_matches_step_path(tiny):
         assert float((v[i, :, :L] - vg[i, :, :L]).abs().max()) <= 1e-4, i
 
 
-def _with_pdl(files, mode):
-    os.environ["Q6W_PDL"] = mode
+def _with_env(files, name, mode):
+    os.environ[name] = mode
     try:
         return Q6WCudaTransformer.from_q6w(*files)
     finally:
-        del os.environ["Q6W_PDL"]
+        del os.environ[name]
+
+
+def _assert_same_generation(x, y, prompts, new_tokens):
+    a = x.generate_greedy(prompts, new_tokens, keep_logits=True)
+    b = y.generate_greedy(prompts, new_tokens, keep_logits=True)
+    assert a.sampled == b.sampled
+    assert torch.equal(a.logits, b.logits)
+    for i, p in enumerate(prompts):
+        P = len(p) + len(a.sampled[i]) - 1  # positions the generation wrote
+        assert torch.equal(a.caches[0][i, :, :P], b.caches[0][i, :, :P]), i
+        assert torch.equal(a.caches[1][i, :, :P], b.caches[1][i, :, :P]), i
+
+
+def test_deep_attention_bit_identical(tiny_files):
+    # ragged prompts of 4..24 tokens, 40 new: lengths up to 63, so both the
+    # even and the odd passes of the two-pass prefetch end the loop
+    deep, shallow = _with_env(tiny_files, "Q6W_ATTN_DEEP", "1"), _with_env(tiny_files, "Q6W_ATTN_DEEP", "0")
+    _assert_same_generation(deep, shallow, _prompts(300, 33, 4, 24, 4096), 40)
 
 
 def test_pdl_step_bit_identical(tiny_files):
-    on, off = _with_pdl(tiny_files, "1"), _with_pdl(tiny_files, "0")
+    on, off = _with_env(tiny_files, "Q6W_PDL", "1"), _with_env(tiny_files, "Q6W_PDL", "0")
     prompts = _prompts(300, 32, 4, 24, 4096)
     a = on.generate_greedy(prompts, 12, keep_logits=True)
     b = off.generate_greedy(prompts, 12, keep_logits=True)
