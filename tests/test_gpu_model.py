@@ -376,3 +376,25 @@ def test_general_tensor_core_step(tmp_path_factory, monkeypatch, n):
             for t in range(T):
                 want = orc.step(int(toks[t, i]), t, ko, vo)
         assert float((a_lg[i] - want).abs().max()) <= LOGIT_TOL, i
+
+
+def test_dim128_wide_hidden_leaves_tensor_core_step(tmp_path_factory):
+    """dim 128 with hidden 512 (multiple_of 256): the packed w2 rows of a
+    128-row residual tile would not fit the tensor-core step's staging area,
+    so the model takes the FP32 SIMT step, token-exact against the oracle."""
+    from torch.profiler import ProfilerActivity, profile
+
+    args = {"dim": 128, "n_layers": 2, "n_heads": 8, "n_kv_heads": 4, "vocab_size": 4096, "multiple_of": 256,
+            "max_seq_len": 64, "dropout": 0.0}
+    b, m = small_model_files(tmp_path_factory, args, 31, "wide_hidden")
+    cuda, orc = Q6WCudaTransformer.from_q6w(b, m), OracleModel.from_q6w(b, m)
+    assert cuda.hidden_dim == 512
+    prompts = _ragged_prompts(96, 31, 4, 20)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        res = cuda.generate_greedy(prompts, 8)
+        torch.cuda.synchronize()
+    names = {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+    assert not any("tc_gemm_kernel" in s for s in names), sorted(names)
+    idx = list(range(0, 96, 8))
+    summary = BatchScorer(orc).verify_greedy([prompts[i] for i in idx], [res.sampled[i] for i in idx], 8)
+    assert summary["failures"] == [], summary["failures"][:5]

@@ -2135,12 +2135,14 @@ static int32_t enqueue_step_pdec(const q6w_model* M, const Work& w, float* kc, f
 }
 
 // Shapes the tensor-core step handles: dim 128, [wq|wk|wv] one N tile of at
-// most 256 rows in 32-row chunks, hidden a multiple of 128, vocab a multiple
-// of 256, and an instantiated streaming-attention layout.
+// most 256 rows in 32-row chunks, hidden a multiple of 128 whose packed w2
+// rows fit the staging area at the widest residual tile (128 rows: hidden at
+// most 384), vocab a multiple of 256, and an instantiated streaming-attention
+// layout.  Wider hidden layers take the general tensor-core step.
 static bool tc_shapes_ok(const q6w_model_desc& d, int hd, int kvr) {
   const int rep = d.n_heads / d.n_kv_heads;
   return d.dim == 128 && kvr % 32 == 0 && d.dim + 2 * kvr <= 256 && d.hidden_dim % 128 == 0 &&
-         d.hidden_dim <= 1024 && d.vocab_size % 256 == 0 && (hd == 16 || hd == 32) && rep <= 4 &&
+         tc::stage_fits(128, d.hidden_dim) && d.vocab_size % 256 == 0 && (hd == 16 || hd == 32) && rep <= 4 &&
          d.n_kv_heads * hd / 16 <= 32;
 }
 

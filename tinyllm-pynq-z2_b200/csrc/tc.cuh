@@ -304,14 +304,20 @@ __host__ __device__ constexpr int threads_for(int epi) {
   return (epi == TEPI_GLU || epi == TEPI_VOCAB || epi == TEPI_RESNORM) ? 512 : kThreads;
 }
 
+// Bytes of the staging area that receives an item's packed weight rows (all
+// of K) and their scales: 128 rows of K = 384.
+constexpr int kStageBytes = 128 * (288 + 4);
+
+// Whether N packed rows of K plus their scales fit the staging area.
+__host__ __device__ constexpr bool stage_fits(int64_t N, int64_t K) { return N * (K * 3 / 4 + 4) <= kStageBytes; }
+
 // Rows per N tile of the plain linear (TEPI_STORE) on this kernel, or 0 when
 // the shape does not fit it: K a multiple of 128, N in {256, 128, 64}
-// dividing rows, and N packed rows of K plus their scales within the
-// 37,376-byte staging area.
+// dividing rows, and the tile's packed rows within the staging area.
 __host__ __device__ inline int store_tile_rows(int64_t rows, int64_t K) {
   if (K <= 0 || K % kKC) return 0;
   for (int N = 256; N >= 64; N >>= 1)
-    if (rows % N == 0 && (int64_t)N * (K * 3 / 4 + 4) <= 128 * (288 + 4)) return N;
+    if (rows % N == 0 && stage_fits(N, K)) return N;
   return 0;
 }
 
@@ -892,7 +898,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
   }
 }
 
-constexpr size_t smem_bytes() { return 1024 + 3 * kM * kKC * 2 + 256 * kKC * 2 + 128 * (288 + 4); }
+constexpr size_t smem_bytes() { return 1024 + 3 * kM * kKC * 2 + 256 * kKC * 2 + kStageBytes; }
 
 }  // namespace tc
 }  // namespace q6w
