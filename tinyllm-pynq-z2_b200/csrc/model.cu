@@ -1409,7 +1409,7 @@ __global__ void embed_tc_kernel(const uint8_t* __restrict__ E, const float* __re
 static int32_t tc_launch(int epi, const tc::TcArgs& a, int sms, cudaStream_t st, bool pdl = false) {
   const int items = ((a.n + tc::kM - 1) / tc::kM) * a.n_tiles;
   const int grid = items < sms ? items : sms;
-  const size_t smem = tc::smem_bytes();
+  const size_t smem = tc::smem_bytes_for(epi);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(tc::threads_for(epi));
@@ -1478,7 +1478,9 @@ static int tc_glu_rows_per_tile(int n, int hid, int sms) {
 static int32_t tc_set_attrs() {
   const int smem = (int)tc::smem_bytes();
   cudaError_t e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_RESNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_RESNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)tc::smem_bytes_for(tc::TEPI_RESNORM));
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_VOCAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc::tc_gemm_kernel<tc::TEPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
   constexpr int NT = threads_for(EPI);
   constexpr int kParts = NT / 128;  // warps reading each TMEM lane quadrant (column parts)
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t mma_bar, ld_bar;
+  __shared__ uint64_t mma_bar, ld_bar, ld_bar1;
   __shared__ uint32_t tmem_base;
   __shared__ __align__(16) float sscale[256];
   __shared__ int timed_out;
@@ -431,7 +431,14 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;                       // [3][2][128][128 B] = 96 KB (one K stage)
   uint8_t* sB = smem + 3 * kM * kKC * 2;    // [2][N][128 B]
-  uint8_t* stage = sB + 256 * kKC * 2;      // packed rows [N][K*3/4] + scales [N]
+  // RESNORM in 32-column tiles (4-CTA clusters, one item a CTA) with more
+  // than one K stage: the A stages alternate between sA and a second buffer
+  // sA1 placed after the 32-row B tile, so the next stage's copy runs under
+  // this stage's expansion and MMAs; the staging area then follows sA1
+  // (smem_bytes_for).
+  const bool dbl = EPI == TEPI_RESNORM && a.pair == 4 && a.K > kKC;
+  uint8_t* sA1 = sB + 32 * kKC * 2;
+  uint8_t* stage = dbl ? sA1 + 3 * kM * kKC * 2 : sB + 256 * kKC * 2;  // packed rows [N][K*3/4] + scales [N]
 
   if (warp == 0) {
     tmem_alloc(&tmem_base, 256);
@@ -440,6 +447,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
   if (tid == 0) {
     mbar_init(&mma_bar, 1);
     mbar_init(&ld_bar, 1);
+    mbar_init(&ld_bar1, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     timed_out = 0;
   }
@@ -454,7 +462,8 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
   const int it0 = blockIdx.x * per, it1 = min(items, it0 + per);
   const int kstages = a.K / kKC;
   const uint32_t rb = (uint32_t)a.K * 3 / 4;
-  uint32_t ph_mma = 0, ph_ld = 0;
+  uint32_t ph_mma = 0, ph_ld = 0, ph_ld1 = 0;
+  int pend0 = 0, pend1 = 0;  // dbl: copies in flight on ld_bar / ld_bar1 (the same in every thread)
   // The weights do not depend on the preceding grid: their copies start
   // before the programmatic-dependency wait, the activation tile after it.
   grid_dep_launch();
@@ -462,6 +471,10 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
     issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 0, false, true, sA, stage, &ld_bar, false);
   grid_dep_wait();
   if (tid == 0 && it0 < it1) issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 0, true, false, sA, stage, &ld_bar);
+  if (dbl && it0 < it1) {
+    if (tid == 0) issue_loads(a, EPI, it0 / a.n_tiles, it0 % a.n_tiles, 1, true, false, sA1, stage, &ld_bar1);
+    pend0 = pend1 = 1;
+  }
 
   for (int it = it0; it < it1 && !timed_out; ++it) {
     const int mt = it / a.n_tiles, nt = it % a.n_tiles;
@@ -510,11 +523,18 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       }
     }
     for (int ks = 0; ks < kstages; ++ks) {
-      if (!mbar_wait(&ld_bar, ph_ld)) {
+      const bool odd = dbl && (ks & 1);  // this stage is in sA1
+      if (!mbar_wait(odd ? &ld_bar1 : &ld_bar, odd ? ph_ld1 : ph_ld)) {
         if (tid == 0) atomicOr(a.err, kErrTimeout);
         timed_out = 1;
       }
-      ph_ld ^= 1;
+      if (odd) {
+        ph_ld1 ^= 1;
+        --pend1;
+      } else {
+        ph_ld ^= 1;
+        if (dbl) --pend0;
+      }
       __syncthreads();
       if (timed_out) break;
       // expand N rows x 128 codes (columns 128ks..) from the staged bytes to bf16
@@ -542,7 +562,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       __syncthreads();
       if (tid == 0) {
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+        const uint32_t a0 = smem_u32(odd ? sA1 : sA), b0 = smem_u32(sB);
 #pragma unroll 1
         for (int p = 0; p < 3; ++p)
 #pragma unroll
@@ -562,7 +582,16 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
       ph_mma ^= 1;
       tc_fence_after();
       // prefetch the next stage / item while this one's epilogue runs
-      if (tid == 0 && !timed_out) {
+      if (dbl) {
+        // the buffer just read takes the stage two ahead
+        if (!timed_out && ks + 2 < kstages) {
+          if (tid == 0) issue_loads(a, EPI, mt, nt, ks + 2, true, false, odd ? sA1 : sA, stage, odd ? &ld_bar1 : &ld_bar);
+          if (odd)
+            ++pend1;
+          else
+            ++pend0;
+        }
+      } else if (tid == 0 && !timed_out) {
         if (ks + 1 < kstages) {
           issue_loads(a, EPI, mt, nt, ks + 1, true, false, sA, stage, &ld_bar);
         } else if (it + 1 < it1) {
@@ -881,6 +910,12 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
     tc_fence_before();
     __syncthreads();
   }
+  // a CTA that stopped on a timed-out wait first waits (bounded) for its A
+  // copies still in flight, so none lands after it exits
+  if (dbl && tid == 0) {
+    if (pend0 > 0) (void)mbar_wait(&ld_bar, ph_ld);
+    if (pend1 > 0) (void)mbar_wait(&ld_bar1, ph_ld1);
+  }
   // a pair CTA that stopped early still takes its two cluster barriers, so
   // the peer's waits end; the second one's wait comes last
   if (EPI == TEPI_RESNORM && a.pair) {
@@ -899,6 +934,15 @@ __global__ void __launch_bounds__(threads_for(EPI), 1) tc_gemm_kernel(TcArgs a) 
 }
 
 constexpr size_t smem_bytes() { return 1024 + 3 * kM * kKC * 2 + 256 * kKC * 2 + kStageBytes; }
+
+// Dynamic shared memory of a kernel: RESNORM also fits the double-buffered
+// layout of its 32-column tiles (two A stages, the 32-row B tile, and 32
+// packed rows of K <= 384 in the staging area after them).
+constexpr size_t smem_bytes_for(int epi) {
+  return epi == TEPI_RESNORM ? 1024 + 2 * 3 * kM * kKC * 2 + 32 * kKC * 2 + 32 * (384 * 3 / 4 + 4) : smem_bytes();
+}
+static_assert(smem_bytes_for(TEPI_RESNORM) >= smem_bytes() && smem_bytes_for(TEPI_RESNORM) <= 232448,
+              "RESNORM shared memory");
 
 }  // namespace tc
 }  // namespace q6w
