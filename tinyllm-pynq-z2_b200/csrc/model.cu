@@ -674,9 +674,11 @@ static bool attn_rows_instantiated(int hd, int KV, int rep) {
 
 // Decode attention, one warp per sequence: the warp streams the sequence's
 // K and V rows 0..T-1 once (32/R rows per pass, R = KV*HD/16 lanes per row,
-// 16 dims per lane), prefetching the next pass's rows while it computes the
-// current one, with an online softmax per lane for the REP query heads of
-// its kv head; lanes holding the same (kv head, dims) merge by shuffles.
+// 16 dims per lane), prefetching the next pass's rows (or the next two
+// passes', at small batches) while it computes the current one, with an
+// online softmax per lane for the REP query heads of its kv head; lanes
+// holding the same (kv head, dims) merge by shuffles.
+
 // One pass of a lane: position t's K and V rows (kv, vv; act: t < T) into
 // the lane's online softmax (m, l, acc) of its REP query heads.
 template <int C, int REP>
